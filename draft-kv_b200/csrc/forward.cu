@@ -1,0 +1,147 @@
+// Whole-decoder forward pass: the native runtime loop over layers.
+//
+// Replaces draftkv/llama.py:175-225 (LlamaLike.forward) and
+// draftkv/gpt2.py:182-213 (GPT2.forward).  The layer loop runs here, in C++,
+// so one call launches every kernel of a forward and the sequence can be
+// captured into one CUDA graph per (shape, config).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dkv {
+size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap, size_t* attn_bytes,
+                    size_t* gemm_bytes);
+}
+
+using namespace dkv;
+
+static int round128(int x) { return (x + 127) / 128 * 128; }
+
+size_t dkv::forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap, size_t* attn_bytes,
+                         size_t* gemm_bytes) {
+    const int N = batch * T;
+    const int elem = m->dtype == DKV_F32 ? 4 : 2;
+    const int HD = m->n_heads * m->d_head, KD = m->n_kv * m->d_head;
+    const int dff_act = m->d_ff;
+    size_t g = 0;
+    g = std::max(g, dkv_gemm_work_bytes(round128(HD + 2 * KD), N, m->d_model, m->dtype));
+    g = std::max(g, dkv_gemm_work_bytes(round128(m->d_model), N, HD, m->dtype));
+    g = std::max(g, dkv_gemm_work_bytes(round128(m->arch == DKV_ARCH_LLAMA ? 2 * m->d_ff : m->d_ff), N, m->d_model,
+                                        m->dtype));
+    g = std::max(g, dkv_gemm_work_bytes(round128(m->d_model), N, m->d_ff, m->dtype));
+    g = std::max(g, dkv_gemm_work_bytes(m->vocab_pad, N, m->d_model, m->dtype));
+    dkv_dims dims{m->n_layers, m->n_kv, m->d_head, batch};
+    const size_t a = dkv_attn_work_bytes(dims, m->n_heads / m->n_kv, T, max_ctx, m->split_keys, comp_cap);
+    if (attn_bytes) *attn_bytes = a;
+    if (gemm_bytes) *gemm_bytes = g;
+    size_t b = 0;
+    b += align_up((size_t)N * m->d_model * 4, 256);                  // h
+    b += align_up((size_t)N * std::max(m->d_model, HD) * elem, 256);  // x / attn out
+    b += align_up((size_t)N * dff_act * elem, 256);                  // act
+    b += align_up((size_t)N * HD * 4, 256);                          // q
+    b += align_up((size_t)N * KD * 2 * elem, 256);                   // kv stage
+    return b + align_up(g, 256) + align_up(a, 256) + 4096;
+}
+
+extern "C" size_t dkv_forward_work_bytes(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap) {
+    if (!m) return 0;
+    return forward_work(m, batch, T, max_ctx, comp_cap, nullptr, nullptr);
+}
+
+extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const dkv_comp_cache* comp,
+                           const dkv_step* st, void* stream) {
+    DKV_REQUIRE(m && st && m->layers && st->tokens && st->pos0 && st->logits, "dkv_forward: bad arguments");
+    DKV_REQUIRE(comp || (full && full->k_pool && full->page_table),
+                "dkv_forward: a full-cache forward needs the full cache");
+    DKV_REQUIRE(m->n_heads % m->n_kv == 0, "dkv_forward: n_heads %% n_kv != 0");
+    DKV_REQUIRE(!comp || st->T == 1, "dkv_forward: draft steps have T == 1");
+    DKV_REQUIRE(st->max_T >= st->T && st->T >= 0, "dkv_forward: T %d > max_T %d", st->T, st->max_T);
+    DKV_REQUIRE(!full || m->dtype == full->dtype, "dkv_forward: model and cache dtypes differ");
+    const int N = st->batch * st->T;
+    if (N == 0) return DKV_OK;
+    const int dm = m->d_model, D = m->d_head, H = m->n_heads, KV = m->n_kv;
+    const int HD = H * D, KD = KV * D;
+    const int elem = m->dtype == DKV_F32 ? 4 : 2;
+    const bool llama = m->arch == DKV_ARCH_LLAMA;
+    size_t attn_bytes = 0, gemm_bytes = 0;
+    // the arena layout depends on (batch, max_T, max_ctx, cap) only, so the
+    // ticket regions stay at fixed offsets across calls with different T
+    const size_t need = forward_work(m, st->batch, st->max_T, st->max_ctx, comp ? comp->cap : 0, &attn_bytes,
+                                     &gemm_bytes);
+    DKV_REQUIRE(st->work && st->work_bytes >= need, "dkv_forward: work buffer %zu < %zu bytes", st->work_bytes, need);
+    const size_t NM = (size_t)st->batch * st->max_T;
+    Arena ar(st->work, st->work_bytes);
+    uint8_t* gwork = ar.take<uint8_t>(gemm_bytes);
+    uint8_t* awork = ar.take<uint8_t>(attn_bytes);
+    float* h = ar.take<float>(NM * dm);
+    uint8_t* x = ar.take<uint8_t>(NM * std::max(dm, HD) * elem);
+    uint8_t* act = ar.take<uint8_t>(NM * m->d_ff * elem);
+    float* q = ar.take<float>(NM * HD);
+    uint8_t* stage = ar.take<uint8_t>(NM * KD * 2 * elem);
+    DKV_REQUIRE(h && x && act && q && stage && gwork && awork, "dkv_forward: arena");
+    dkv_dims dims{m->n_layers, KV, D, st->batch};
+    const int group = H / KV;
+
+    DKV_TRY(dkv_embed(m->tok_emb, m->dtype, m->pos_emb, st->tokens, st->tok_stride, st->batch, st->T, st->pos0, dm,
+                      m->vocab, m->max_pos, h, stream));
+    for (int L = 0; L < m->n_layers; ++L) {
+        const dkv_layer& ly = m->layers[L];
+        DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n1_w, ly.n1_b, m->eps, x, m->dtype, stream));
+        dkv_epilogue e{};
+        e.kind = DKV_EPI_QKV;
+        e.bias = ly.b_qkv;
+        e.act_dtype = m->dtype;
+        e.n_heads = H;
+        e.n_kv = KV;
+        e.d_head = D;
+        e.tokens_per_seq = st->T;
+        e.pos0 = st->pos0;
+        e.rope_cos = llama ? m->rope_cos : nullptr;
+        e.rope_sin = llama ? m->rope_sin : nullptr;
+        e.q_out = q;
+        e.kv_stage = comp ? stage : nullptr;
+        e.full = full;
+        e.layer = L;
+        e.n_layers = m->n_layers;
+        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_qkv, m->dtype, round128(HD + 2 * KD), N, dm, &e, gwork, gemm_bytes, stream));
+        if (comp) {
+            DKV_TRY(dkv_comp_append(comp, full, dims, L, 1, stage, m->dtype, 1, st->pos0, nullptr, nullptr, L == 0 ? 1 : 0,
+                                    stream));
+            DKV_TRY(dkv_attn_comp(comp, dims, L, group, q, st->pos0, x, m->dtype, awork, attn_bytes, stream));
+        } else {
+            DKV_TRY(dkv_attn_full(full, dims, L, group, st->T, q, st->pos0, x, m->dtype, m->split_keys, awork,
+                                  attn_bytes, stream));
+        }
+        dkv_epilogue eo{};
+        eo.kind = DKV_EPI_RESADD;
+        eo.bias = ly.b_o;
+        eo.out_f32 = h;
+        eo.ld_out = dm;
+        eo.act_dtype = m->dtype;
+        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_o, m->dtype, round128(dm), N, HD, &eo, gwork, gemm_bytes, stream));
+        DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n2_w, ly.n2_b, m->eps, x, m->dtype, stream));
+        dkv_epilogue eu{};
+        eu.kind = llama ? DKV_EPI_SWIGLU : DKV_EPI_GELU;
+        eu.bias = ly.b_up;
+        eu.act = act;
+        eu.act_dtype = m->dtype;
+        eu.ld_out = m->d_ff;
+        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_up, m->dtype, round128(llama ? 2 * m->d_ff : m->d_ff), N, dm, &eu, gwork,
+                         gemm_bytes, stream));
+        dkv_epilogue ed{};
+        ed.kind = DKV_EPI_RESADD;
+        ed.bias = ly.b_down;
+        ed.out_f32 = h;
+        ed.ld_out = dm;
+        ed.act_dtype = m->dtype;
+        DKV_TRY(dkv_gemm(act, m->dtype, ly.w_down, m->dtype, round128(dm), N, m->d_ff, &ed, gwork, gemm_bytes, stream));
+    }
+    DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, m->nf_w, m->nf_b, m->eps, x, m->dtype, stream));
+    dkv_epilogue eh{};
+    eh.kind = DKV_EPI_STORE;
+    eh.out_f32 = st->logits;
+    eh.ld_out = m->vocab;
+    eh.act_dtype = m->dtype;
+    DKV_TRY(dkv_gemm(x, m->dtype, m->w_head, m->dtype, m->vocab_pad, N, dm, &eh, gwork, gemm_bytes, stream));
+    return DKV_OK;
+}

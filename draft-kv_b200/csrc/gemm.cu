@@ -1,0 +1,514 @@
+// K4 weight-streaming GEMM (Y = X W^T) and K4e fused epilogues.
+//
+// Replaces the projections of draftkv/llama.py:187-225 (x @ W.T, SwiGLU :222,
+// tied head :224-225, RoPE :197-198 with _rope :164-172) and
+// draftkv/gpt2.py:191-213 (Conv1D x @ W + b, gelu_new :126-127, tied head).
+//
+// Decode-time GEMMs have few tokens (N = batch x (gamma+1) <= 64 per CTA)
+// and stream every weight byte once, so the kernel is organised around the
+// weight stream: weights are stored in a tiled layout where one warp-wide
+// 16-byte load per k-step yields exactly the mma.m16n8k16 A fragments
+// (512 contiguous bytes per warp per k-step), weight rows ride on M and the
+// tokens on N ("swap-AB").  Tokens are staged in shared memory in 128-wide k
+// chunks and fed through ldmatrix.
+//
+// Determinism / batch invariance: the split of K across CTAs (S) depends
+// only on (M, K), partial sums are reduced in a fixed order by the last CTA
+// of each row tile (atomic ticket, no spin), and a token's column never
+// depends on the other columns, so a token's output is bit-identical whether
+// it is computed with 1 or 64 other tokens.  This is what makes the verify
+// pass reproduce plain decoding exactly.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dkv {
+
+constexpr int kTileM = 128;     // weight rows per CTA (8 warps x 16)
+constexpr int kChunkK = 128;    // k elements per staged X chunk
+constexpr int kTileStride = 132;  // smem row stride (floats) of the result tile [n][m]
+// Split-K tickets occupy a fixed region at the start of every GEMM work
+// buffer, so consecutive calls of any shape see them zero (each launch
+// resets the tickets it used).
+constexpr size_t kGemmTickets = 65536;
+
+struct EpiArgs {
+    int kind;
+    const float* bias;
+    float* out_f32;
+    void* act;
+    int act_dtype, ld_out, M_real;
+    int n_heads, n_kv, d_head, tokens_per_seq;
+    const int32_t* pos0;
+    const float* rope_cos;
+    const float* rope_sin;
+    float* q_out;
+    void* kv_stage;
+    int model_dtype;
+    // full cache target
+    void* k_pool;
+    void* v_pool;
+    const int32_t* page_table;
+    int page_size, max_pages, layer, n_layers;
+};
+
+DKV_DEV float gelu_new(float x) {
+    // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))  (gpt2.py:126-127)
+    return 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+}
+
+DKV_DEV float silu(float x) { return x / (1.0f + expf(-x)); }
+
+// Applies the epilogue to the tile T[n][m] (n < nb valid tokens starting at n0).
+DKV_DEV void run_epilogue(const EpiArgs& e, const float* T, int mtile, int n0, int nb) {
+    const int m0 = mtile * kTileM;
+    const int total = kTileM * nb;
+    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+        const int i = idx % kTileM, j = idx / kTileM;
+        const int m = m0 + i, n = n0 + j;
+        const float acc = T[j * kTileStride + i];
+        switch (e.kind) {
+            case DKV_EPI_STORE:
+                if (m < e.M_real) e.out_f32[(size_t)n * e.ld_out + m] = acc + (e.bias ? e.bias[m] : 0.f);
+                break;
+            case DKV_EPI_RESADD:
+                if (m < e.M_real) e.out_f32[(size_t)n * e.ld_out + m] += acc + (e.bias ? e.bias[m] : 0.f);
+                break;
+            case DKV_EPI_GELU:
+                if (m < e.M_real)
+                    store_from_f32(e.act, e.act_dtype, (size_t)n * e.ld_out + m,
+                                   gelu_new(acc + (e.bias ? e.bias[m] : 0.f)));
+                break;
+            case DKV_EPI_SWIGLU:
+                if (i < 64) {
+                    const float g = acc + (e.bias ? e.bias[m] : 0.f);
+                    const float u = T[j * kTileStride + i + 64] + (e.bias ? e.bias[m + 64] : 0.f);
+                    const int col = mtile * 64 + i;
+                    if (col < e.M_real) store_from_f32(e.act, e.act_dtype, (size_t)n * e.ld_out + col, silu(g) * u);
+                }
+                break;
+            case DKV_EPI_QKV: {
+                const int D = e.d_head, HD = e.n_heads * D, KD = e.n_kv * D;
+                if (m >= HD + 2 * KD) break;
+                const int b = n / e.tokens_per_seq, t = n % e.tokens_per_seq;
+                const int p = e.pos0[b] + t;
+                const int sec = m < HD ? 0 : (m < HD + KD ? 1 : 2);
+                const int mm = sec == 0 ? m : (sec == 1 ? m - HD : m - HD - KD);
+                const int head = mm / D, dd = mm % D;
+                float val = acc + (e.bias ? e.bias[m] : 0.f);
+                if (sec < 2 && e.rope_cos) {
+                    const int hd = D / 2;
+                    const int pair = dd < hd ? i + hd : i - hd;
+                    const float other = T[j * kTileStride + pair] + (e.bias ? e.bias[m0 + pair] : 0.f);
+                    const int f = dd < hd ? dd : dd - hd;
+                    const float cs = e.rope_cos[(size_t)p * hd + f], sn = e.rope_sin[(size_t)p * hd + f];
+                    // x*cos + rotate_half(x)*sin, rotate_half = [-x2, x1]
+                    val = dd < hd ? val * cs - other * sn : val * cs + other * sn;
+                }
+                if (sec == 0) {
+                    e.q_out[(size_t)n * HD + mm] = val;
+                } else if (e.kv_stage) {
+                    const size_t o = (((size_t)n * e.n_kv + head) * 2 + (sec - 1)) * D + dd;
+                    store_from_f32(e.kv_stage, e.model_dtype, o, val);
+                } else {
+                    const int page = e.page_table[((size_t)b * e.n_layers + e.layer) * e.max_pages + p / e.page_size];
+                    const size_t o = (((size_t)page * e.n_kv + head) * e.page_size + (p % e.page_size)) * D + dd;
+                    store_from_f32(sec == 1 ? e.k_pool : e.v_pool, e.model_dtype, o, val);
+                }
+                break;
+            }
+            default:
+                break;
+        }
+    }
+}
+
+// Split-K finish: every CTA of a row tile leaves its partial tile; the last to
+// arrive sums them in split order and runs the epilogue.
+DKV_DEV void finish_tile(const EpiArgs& e, float* tile, int nbc, int mtile, int mtiles, int nblk_idx, int S,
+                         int s, int n0, int nb, float* ws, unsigned* tickets) {
+    const int tile_floats = nbc * kTileStride;
+    if (S > 1) {
+        float* mine = ws + (((size_t)nblk_idx * mtiles + mtile) * S + s) * tile_floats;
+        for (int i = threadIdx.x; i < tile_floats; i += blockDim.x) mine[i] = tile[i];
+        __threadfence();
+        __syncthreads();
+        __shared__ int is_last;
+        if (threadIdx.x == 0) {
+            unsigned* tk = tickets + (size_t)nblk_idx * mtiles + mtile;
+            const unsigned prev = atomicAdd(tk, 1u);
+            is_last = prev == (unsigned)(S - 1);
+            if (is_last) *tk = 0u;   // self-reset for the next launch
+        }
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
+        const float* base = ws + (((size_t)nblk_idx * mtiles + mtile) * S) * tile_floats;
+        for (int i = threadIdx.x; i < tile_floats; i += blockDim.x) {
+            float acc = __ldcg(base + i);
+            for (int q = 1; q < S; ++q) acc += __ldcg(base + (size_t)q * tile_floats + i);
+            tile[i] = acc;
+        }
+        __syncthreads();
+    }
+    run_epilogue(e, tile, mtile, n0, nb);
+}
+
+struct GemmArgs {
+    const void* x;      // [N][K] bf16 or f32
+    const void* w;      // tiled bf16 or row-major f32
+    int M, N, K, S;
+    float* ws;
+    unsigned* tickets;
+    EpiArgs epi;
+};
+
+DKV_DEV void mma_bf16(float (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+DKV_DEV void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a));
+}
+DKV_DEV void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+
+DKV_DEV void cp_async16(void* smem, const void* gmem, bool pred) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    const int n = pred ? 16 : 0;   // zero-fill when out of range
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+DKV_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+DKV_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// X chunk row stride in bf16 elements (128 + 8 padding: conflict-free ldmatrix)
+constexpr int kXStride = kChunkK + 8;
+
+template <int NT>   // number of n8 token tiles per CTA (tokens = 8*NT)
+__global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
+    extern __shared__ __align__(16) uint8_t gsm[];
+    constexpr int NB = 8 * NT;
+    uint16_t* xs = reinterpret_cast<uint16_t*>(gsm);          // [2][NB][kXStride]
+    const int mtiles = g.M / kTileM;
+    const int mtile = blockIdx.x % mtiles, s = blockIdx.x / mtiles;
+    const int nblk = blockIdx.y, n0 = nblk * 64;
+    const int KT = g.K / 16;
+    const int kt0 = (int)((long long)s * KT / g.S), kt1 = (int)((long long)(s + 1) * KT / g.S);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint16_t* X = reinterpret_cast<const uint16_t*>(g.x);
+
+    // X chunk loader: rows n0..n0+NB-1, k range [k_lo, k_lo + 128)
+    auto load_chunk = [&](int buf, int k_lo) {
+        uint16_t* dst = xs + buf * NB * kXStride;
+        for (int i = threadIdx.x; i < NB * (kChunkK / 8); i += blockDim.x) {
+            const int r = i / (kChunkK / 8), c8 = i % (kChunkK / 8);
+            const int n = n0 + r, k = k_lo + c8 * 8;
+            const bool ok = n < g.N && k < kt1 * 16;
+            cp_async16(dst + r * kXStride + c8 * 8, ok ? (const void*)(X + (size_t)n * g.K + k) : (const void*)X, ok);
+        }
+        cp_async_commit();
+    };
+
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+
+    const uint4* W = reinterpret_cast<const uint4*>(g.w) + ((size_t)(mtile * 8 + warp) * KT) * 32 + lane;
+    constexpr int PF = 8;
+    uint4 ring[PF];
+#pragma unroll
+    for (int i = 0; i < PF; ++i)
+        if (kt0 + i < kt1) ring[i] = __ldcs(W + (size_t)(kt0 + i) * 32);
+
+    const int nchunks = (kt1 - kt0 + 7) / 8;
+    if (nchunks > 0) load_chunk(0, kt0 * 16);
+    for (int ch = 0; ch < nchunks; ++ch) {
+        if (ch + 1 < nchunks) {
+            load_chunk((ch + 1) & 1, (kt0 + (ch + 1) * 8) * 16);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const uint16_t* xb = xs + (ch & 1) * NB * kXStride;
+#pragma unroll
+        for (int i = 0; i < PF; ++i) {
+            const int kt = kt0 + ch * 8 + i;
+            if (kt < kt1) {
+                const uint4 a = ring[i];
+                if (kt + PF < kt1) ring[i] = __ldcs(W + (size_t)(kt + PF) * 32);
+                const int kc = i * 16;   // k offset within chunk
+#pragma unroll
+                for (int j = 0; j + 1 < NT; j += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    const int mi = lane >> 3, r = lane & 7;
+                    const uint16_t* p = xb + (8 * j + (mi >= 2 ? 8 : 0) + r) * kXStride + kc + (mi & 1) * 8;
+                    ldsm_x4(b0, b1, b2, b3, p);
+                    mma_bf16(acc[j], a, b0, b1);
+                    mma_bf16(acc[j + 1], a, b2, b3);
+                }
+                if (NT & 1) {
+                    uint32_t b0, b1;
+                    const int mi = (lane >> 3) & 1, r = lane & 7;
+                    const uint16_t* p = xb + (8 * (NT - 1) + r) * kXStride + kc + mi * 8;
+                    ldsm_x2(b0, b1, p);
+                    mma_bf16(acc[NT - 1], a, b0, b1);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // result tile T[n][m] in shared memory (reuses the X buffers)
+    float* tile = reinterpret_cast<float*>(gsm);
+    {
+        const int r = lane >> 2, c = lane & 3;
+        const int mrow = warp * 16 + r;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            const int n = 8 * j + 2 * c;
+            tile[n * kTileStride + mrow] = acc[j][0];
+            tile[(n + 1) * kTileStride + mrow] = acc[j][1];
+            tile[n * kTileStride + mrow + 8] = acc[j][2];
+            tile[(n + 1) * kTileStride + mrow + 8] = acc[j][3];
+        }
+    }
+    __syncthreads();
+    const int nb = min(NB, g.N - n0);
+    finish_tile(g.epi, tile, NB, mtile, mtiles, nblk, g.S, s, n0, nb, g.ws, g.tickets);
+}
+
+// fp32 weights [M][K] row-major, CUDA cores.  Warp w owns 16 weight rows of
+// the tile; lanes split k in float4 steps; 4 tokens per CTA; warp sums
+// reduced in a fixed butterfly.
+constexpr int kF32Tok = 4;
+constexpr int kF32Chunk = 256;
+
+__global__ void __launch_bounds__(256) gemm_f32_kernel(GemmArgs g) {
+    extern __shared__ __align__(16) uint8_t gsm[];
+    float* xs = reinterpret_cast<float*>(gsm);   // [kF32Tok][kF32Chunk]
+    const int mtiles = g.M / kTileM;
+    const int mtile = blockIdx.x % mtiles, s = blockIdx.x / mtiles;
+    const int nblk = blockIdx.y, n0 = nblk * kF32Tok;
+    const int KT = g.K / 16;
+    const int k0 = (int)((long long)s * KT / g.S) * 16, k1 = (int)((long long)(s + 1) * KT / g.S) * 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* X = reinterpret_cast<const float*>(g.x);
+    const float* W = reinterpret_cast<const float*>(g.w);
+    float acc[16][kF32Tok];
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Tok; ++t) acc[r][t] = 0.f;
+
+    for (int kc = k0; kc < k1; kc += kF32Chunk) {
+        const int kl = min(kF32Chunk, k1 - kc);
+        __syncthreads();
+        for (int i = threadIdx.x; i < kF32Tok * kF32Chunk; i += blockDim.x) {
+            const int t = i / kF32Chunk, k = i % kF32Chunk;
+            const int n = n0 + t;
+            xs[i] = (n < g.N && k < kl) ? X[(size_t)n * g.K + kc + k] : 0.f;
+        }
+        __syncthreads();
+        for (int k4 = lane; k4 * 4 < kl; k4 += 32) {
+            float4 xv[kF32Tok];
+#pragma unroll
+            for (int t = 0; t < kF32Tok; ++t) xv[t] = *reinterpret_cast<const float4*>(xs + t * kF32Chunk + k4 * 4);
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const int m = mtile * kTileM + warp * 16 + r;
+                const float4 w = __ldcs(reinterpret_cast<const float4*>(W + (size_t)m * g.K + kc) + k4);
+#pragma unroll
+                for (int t = 0; t < kF32Tok; ++t)
+                    acc[r][t] += w.x * xv[t].x + w.y * xv[t].y + w.z * xv[t].z + w.w * xv[t].w;
+            }
+        }
+    }
+    __syncthreads();
+    float* tile = reinterpret_cast<float*>(gsm);
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+#pragma unroll
+        for (int t = 0; t < kF32Tok; ++t) {
+            const float v = warp_sum(acc[r][t]);
+            if (lane == 0) tile[t * kTileStride + warp * 16 + r] = v;
+        }
+    __syncthreads();
+    const int nb = min(kF32Tok, g.N - n0);
+    finish_tile(g.epi, tile, kF32Tok, mtile, mtiles, nblk, g.S, s, n0, nb, g.ws, g.tickets);
+}
+
+// Tiles W [M][K] bf16 into the A-fragment layout [M/16][K/16][32][8].
+__global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int M, int K, uint16_t* __restrict__ out) {
+    const size_t total = (size_t)M * K;
+    for (size_t o = (size_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
+        const int e = o & 7;
+        const int lane = (o >> 3) & 31;
+        const size_t tk = o >> 8;           // (mt16 * KT + kt)
+        const int KT = K / 16;
+        const int kt = (int)(tk % KT);
+        const int mt = (int)(tk / KT);
+        const int reg = e >> 1, el = e & 1;
+        const int r = lane >> 2, c = lane & 3;
+        const int row = mt * 16 + r + ((reg & 1) ? 8 : 0);
+        const int col = kt * 16 + 2 * c + ((reg & 2) ? 8 : 0) + el;
+        out[o] = w[(size_t)row * K + col];
+    }
+}
+
+int choose_split(int M, int K) {
+    const int mtiles = M / kTileM;
+    const int KT = K / 16;
+    int S = (2 * 148 + mtiles / 2) / (mtiles > 0 ? mtiles : 1);
+    if (S < 1) S = 1;
+    const int max_s = KT / 8 > 0 ? KT / 8 : 1;
+    if (S > max_s) S = max_s;
+    return S;
+}
+
+}  // namespace dkv
+
+using namespace dkv;
+
+namespace dkv {
+EpiArgs make_epi(const dkv_epilogue* e, int M_real);
+}
+
+dkv::EpiArgs dkv::make_epi(const dkv_epilogue* e, int M_real) {
+    EpiArgs a{};
+    a.kind = e->kind;
+    a.bias = e->bias;
+    a.out_f32 = e->out_f32;
+    a.act = e->act;
+    a.act_dtype = e->act_dtype;
+    a.ld_out = e->ld_out;
+    a.M_real = M_real;
+    a.n_heads = e->n_heads;
+    a.n_kv = e->n_kv;
+    a.d_head = e->d_head;
+    a.tokens_per_seq = e->tokens_per_seq > 0 ? e->tokens_per_seq : 1;
+    a.pos0 = e->pos0;
+    a.rope_cos = e->rope_cos;
+    a.rope_sin = e->rope_sin;
+    a.q_out = e->q_out;
+    a.kv_stage = e->kv_stage;
+    a.model_dtype = e->act_dtype;
+    a.layer = e->layer;
+    a.n_layers = e->n_layers;
+    if (e->full) {
+        a.k_pool = e->full->k_pool;
+        a.v_pool = e->full->v_pool;
+        a.page_table = e->full->page_table;
+        a.page_size = e->full->page_size;
+        a.max_pages = e->full->max_pages;
+        a.model_dtype = e->full->dtype;
+    }
+    return a;
+}
+
+extern "C" size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    const int mtiles = (M + kTileM - 1) / kTileM;
+    const int S = choose_split(mtiles * kTileM, K);
+    const int tok = w_dtype == DKV_F32 ? kF32Tok : 64;
+    const int nblk = (N + tok - 1) / tok;
+    const size_t tile = (size_t)tok * kTileStride * sizeof(float);
+    size_t b = kGemmTickets * sizeof(unsigned);
+    if (S > 1) b += (size_t)nblk * mtiles * S * tile;
+    return b + 256;
+}
+
+extern "C" int dkv_pack_weight(const uint16_t* w, int M, int K, uint16_t* tiled, void* stream) {
+    DKV_REQUIRE(w && tiled && M > 0 && K > 0, "dkv_pack_weight args");
+    DKV_REQUIRE(M % 16 == 0 && K % 16 == 0, "dkv_pack_weight: M, K must be multiples of 16 (M=%d K=%d)", M, K);
+    pack_weight_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(w, M, K, tiled);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+
+extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K,
+                        const dkv_epilogue* epi, void* work, size_t work_bytes, void* stream) {
+    DKV_REQUIRE(x && w && epi && M > 0 && N >= 0 && K > 0, "dkv_gemm: bad arguments");
+    DKV_REQUIRE(x_dtype == w_dtype, "dkv_gemm: x and w dtypes must match");
+    DKV_REQUIRE(M % kTileM == 0, "dkv_gemm: M (%d) must be padded to a multiple of 128", M);
+    DKV_REQUIRE(K % 16 == 0, "dkv_gemm: K (%d) must be a multiple of 16", K);
+    if (N == 0) return DKV_OK;
+    const int mtiles = M / kTileM;
+    const int S = choose_split(M, K);
+    const int tok = w_dtype == DKV_F32 ? kF32Tok : 64;
+    const int nblk = (N + tok - 1) / tok;
+    DKV_REQUIRE((size_t)nblk * mtiles <= kGemmTickets, "dkv_gemm: too many row tiles x token blocks");
+    Arena ar(work, work_bytes);
+    GemmArgs g;
+    g.x = x;
+    g.w = w;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.S = S;
+    g.tickets = ar.take<unsigned>(kGemmTickets);
+    const size_t tile_floats = (size_t)tok * kTileStride;
+    g.ws = S > 1 ? ar.take<float>((size_t)nblk * mtiles * S * tile_floats) : nullptr;
+    DKV_REQUIRE(g.tickets && (S == 1 || g.ws), "dkv_gemm: work buffer too small (%zu bytes, need %zu)", work_bytes,
+                dkv_gemm_work_bytes(M, N, K, w_dtype));
+    // columns written: m < min(M, ld_out) (the head is padded to 128 rows;
+    // SwiGLU writes d_ff = ld_out columns from 2*d_ff rows)
+    int M_real = M;
+    if (epi->kind != DKV_EPI_QKV) {
+        DKV_REQUIRE(epi->ld_out > 0, "dkv_gemm: ld_out required");
+        M_real = std::min(M, epi->ld_out);
+    }
+    g.epi = make_epi(epi, M_real);
+    if (epi->kind == DKV_EPI_QKV) {
+        DKV_REQUIRE(epi->q_out && epi->pos0 && epi->d_head > 0 && kTileM % epi->d_head == 0,
+                    "dkv_gemm QKV: q_out/pos0 required and d_head must divide 128");
+        DKV_REQUIRE(epi->kv_stage || (epi->full && epi->full->k_pool), "dkv_gemm QKV: no K/V destination");
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    dim3 grid(mtiles * S, nblk);
+    if (w_dtype == DKV_F32) {
+        const size_t smem = std::max((size_t)kF32Tok * kF32Chunk * 4, (size_t)kF32Tok * kTileStride * 4);
+        gemm_f32_kernel<<<grid, 256, smem, st>>>(g);
+        DKV_LAUNCHED();
+        return DKV_OK;
+    }
+    const int nt = std::min(8, (std::min(N, 64) + 7) / 8);
+    const size_t smem_x = (size_t)2 * 8 * nt * kXStride * 2;
+    const size_t smem_t = (size_t)8 * nt * kTileStride * 4;
+    const size_t smem = std::max(smem_x, smem_t);
+#define DKV_GEMM_CASE(NTV)                                                              \
+    case NTV: {                                                                         \
+        static bool attr = false;                                                       \
+        if (!attr) {                                                                    \
+            DKV_CUDA(allow_smem(gemm_bf16_kernel<NTV>, 64 * 1024));                     \
+            attr = true;                                                                \
+        }                                                                               \
+        gemm_bf16_kernel<NTV><<<grid, 256, smem, st>>>(g);                              \
+        break;                                                                          \
+    }
+    switch (nt) {
+        DKV_GEMM_CASE(1)
+        DKV_GEMM_CASE(2)
+        DKV_GEMM_CASE(3)
+        DKV_GEMM_CASE(4)
+        DKV_GEMM_CASE(5)
+        DKV_GEMM_CASE(6)
+        DKV_GEMM_CASE(7)
+        DKV_GEMM_CASE(8)
+        default:
+            return DKV_EINVAL;
+    }
+#undef DKV_GEMM_CASE
+    DKV_LAUNCHED();
+    return DKV_OK;
+}

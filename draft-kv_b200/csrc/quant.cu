@@ -1,0 +1,959 @@
+// K1 quantize / pack, K6 evict, K7 truncate + resync + rebuild of the drafter
+// cache, and plain writes / reads of the full cache.
+//
+// Reference behaviour followed (aabhimittal/Draft-KV):
+//   quantize              draftkv/compress.py:21-46
+//   CompressedKVCache     draftkv/compress.py:95-241  (append :122-133,
+//                         budget :154-157, _evict :159-179, truncate :181-188,
+//                         sync_from :190-207, rebuild_layers :209-230)
+//   FullKVCache / paged   draftkv/compress.py:49-92, draftkv/paged.py:76-177
+#include "common.cuh"
+
+namespace dkv {
+
+// --------------------------------------------------------------------------
+// Exact group quantization of one 64-wide group held by a warp: lane l owns
+// elements 64g+l and 64g+32+l (zero beyond d, as numpy pads).  All ops are
+// IEEE round-to-nearest without contraction, reproducing numpy bit for bit.
+struct GroupQ {
+    float lo, scale;
+};
+
+DKV_DEV GroupQ group_params(float a, float b, int bits) {
+    float lo = warp_min(fminf(a, b));
+    float hi = warp_max(fmaxf(a, b));
+    float levels = (float)((1 << bits) - 1);
+    float scale = __fdiv_rn(__fsub_rn(hi, lo), levels);
+    scale = fmaxf(scale, 1e-8f);
+    return {lo, scale};
+}
+
+DKV_DEV float code_of(float x, GroupQ g, int bits) {
+    float q = rintf(__fdiv_rn(__fsub_rn(x, g.lo), g.scale));
+    q = fminf(fmaxf(q, 0.f), (float)((1 << bits) - 1));
+    return q;
+}
+
+DKV_DEV float deq_of(float q, GroupQ g) { return __fadd_rn(__fmul_rn(q, g.scale), g.lo); }
+
+// One warp per (row, group).
+__global__ void quantize_exact_kernel(const float* __restrict__ x, int64_t rows, int d, int bits,
+                                      uint8_t* __restrict__ codes, float* __restrict__ scale,
+                                      float* __restrict__ lo, float* __restrict__ deq) {
+    const int ng = (d + 63) / 64;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= rows * ng) return;
+    const int64_t r = warp / ng;
+    const int g = (int)(warp % ng);
+    const int e0 = 64 * g + lane, e1 = e0 + 32;
+    float a = e0 < d ? x[r * d + e0] : 0.f;
+    float b = e1 < d ? x[r * d + e1] : 0.f;
+    if (bits >= 16) {
+        if (deq) {
+            if (e0 < d) deq[r * d + e0] = a;
+            if (e1 < d) deq[r * d + e1] = b;
+        }
+        return;
+    }
+    GroupQ gq = group_params(a, b, bits);
+    float qa = code_of(a, gq, bits), qb = code_of(b, gq, bits);
+    if (codes) {
+        codes[r * ng * 64 + e0] = (uint8_t)qa;
+        codes[r * ng * 64 + e1] = (uint8_t)qb;
+    }
+    if (lane == 0) {
+        if (scale) scale[r * ng + g] = gq.scale;
+        if (lo) lo[r * ng + g] = gq.lo;
+    }
+    if (deq) {
+        if (e0 < d) deq[r * d + e0] = deq_of(qa, gq);
+        if (e1 < d) deq[r * d + e1] = deq_of(qb, gq);
+    }
+}
+
+// --------------------------------------------------------------------------
+// Storage order of the drafter cache (see oracle/quant.py): K vectors in the
+// tensor-core fragment order, V vectors in element order.
+DKV_DEV int storage_elem(int p, int d, bool k_order) {
+    if (!k_order) return p;
+    const int q4 = d >> 2;
+    const int c = p / q4, rem = p - c * q4;
+    const int j = rem >> 2, r = rem & 3;
+    return 16 * j + 2 * c + (r & 1) + ((r >> 1) << 3);
+}
+
+// Quantizes and packs one d-element vector with one warp.  `src` is read
+// through load_as_f32 (element stride 1).  `scratch` holds d bytes (warp
+// private).  Writes cb = d*bits/8 bytes of codes and d/64 (scale, lo) fp16
+// pairs; bits == 16 stores the raw elements (in `raw_dtype`) instead.
+DKV_DEV void quant_pack_vector(const void* src, int src_dtype, size_t src_off, int d, int bits,
+                               bool k_order, uint8_t* __restrict__ dst_codes,
+                               uint16_t* __restrict__ dst_sl, int raw_dtype,
+                               uint8_t* scratch) {
+    const int lane = threadIdx.x & 31;
+    if (bits == 16) {
+        for (int p = lane; p < d; p += 32) {
+            float v = load_as_f32(src, src_dtype, src_off + storage_elem(p, d, k_order));
+            store_from_f32(dst_codes, raw_dtype, p, v);
+        }
+        return;
+    }
+    const int ng = d >> 6;
+    for (int g = 0; g < ng; ++g) {
+        const int e0 = 64 * g + lane, e1 = e0 + 32;
+        float a = load_as_f32(src, src_dtype, src_off + e0);
+        float b = load_as_f32(src, src_dtype, src_off + e1);
+        GroupQ gq = group_params(a, b, bits);
+        scratch[e0] = (uint8_t)code_of(a, gq, bits);
+        scratch[e1] = (uint8_t)code_of(b, gq, bits);
+        if (lane == 0) {
+            dst_sl[2 * g] = f32_to_half_bits(gq.scale);
+            dst_sl[2 * g + 1] = f32_to_half_bits(gq.lo);
+        }
+    }
+    __syncwarp();
+    uint32_t* out = reinterpret_cast<uint32_t*>(dst_codes);
+    if (bits == 8) {
+        for (int w = lane; w < d / 4; w += 32) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v |= (uint32_t)scratch[storage_elem(4 * w + i, d, k_order)] << (8 * i);
+            out[w] = v;
+        }
+    } else if (bits == 4 || bits == 2) {
+        const int per = 32 / bits, half = per / 2;
+        for (int w = lane; w < d / per; w += 32) {
+            uint32_t v = 0;
+            for (int i = 0; i < half; ++i) {
+                v |= (uint32_t)scratch[storage_elem(per * w + 2 * i, d, k_order)] << (bits * i);
+                v |= (uint32_t)scratch[storage_elem(per * w + 2 * i + 1, d, k_order)] << (16 + bits * i);
+            }
+            out[w] = v;
+        }
+    } else {  // 3 bit: plane A (low 2 bits, 2-bit layout) then plane B (high bit)
+        for (int w = lane; w < d / 16; w += 32) {
+            uint32_t v = 0;
+            for (int i = 0; i < 8; ++i) {
+                v |= ((uint32_t)scratch[storage_elem(16 * w + 2 * i, d, k_order)] & 3u) << (2 * i);
+                v |= ((uint32_t)scratch[storage_elem(16 * w + 2 * i + 1, d, k_order)] & 3u) << (16 + 2 * i);
+            }
+            out[w] = v;
+        }
+        uint16_t* units = reinterpret_cast<uint16_t*>(dst_codes + d / 4);
+        for (int u = lane; u < d / 16; u += 32) {
+            uint32_t v = 0;
+            for (int i = 0; i < 8; ++i) {
+                v |= ((uint32_t)scratch[storage_elem(16 * u + 2 * i, d, k_order)] >> 2) << i;
+                v |= ((uint32_t)scratch[storage_elem(16 * u + 2 * i + 1, d, k_order)] >> 2) << (8 + i);
+            }
+            units[u] = (uint16_t)v;
+        }
+    }
+    __syncwarp();
+}
+
+// Dequantizes element e of a stored vector (test read-back path).
+DKV_DEV float dequant_elem(const uint8_t* codes, const uint16_t* sl, int d, int bits, bool k_order,
+                           int e, int raw_dtype) {
+    // find the storage position p holding element e
+    int p = e;
+    if (k_order) {
+        const int q4 = d >> 2;
+        const int j = e >> 4, w = e & 15;
+        const int c = (w & 7) >> 1;
+        const int r = (w & 1) | ((w >> 3) << 1);
+        p = c * q4 + 4 * j + r;
+    }
+    if (bits == 16) return load_as_f32(codes, raw_dtype, p);
+    uint32_t q;
+    if (bits == 8) {
+        q = codes[p];
+    } else if (bits == 4 || bits == 2) {
+        const int per = 32 / bits;
+        const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[p / per];
+        const int i = (p % per) >> 1;
+        const int sh = (p & 1) ? 16 + bits * i : bits * i;
+        q = (w >> sh) & ((1u << bits) - 1);
+    } else {
+        const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[p / 16];
+        const int i = (p % 16) >> 1;
+        const int sh = (p & 1) ? 16 + 2 * i : 2 * i;
+        const uint32_t lo2 = (w >> sh) & 3u;
+        const uint16_t u = reinterpret_cast<const uint16_t*>(codes + d / 4)[p / 16];
+        const int sh1 = (p & 1) ? 8 + i : i;
+        q = lo2 | (((u >> sh1) & 1u) << 2);
+    }
+    const int g = e >> 6;
+    float scale = half_bits_to_f32(sl[2 * g]), lo = half_bits_to_f32(sl[2 * g + 1]);
+    return (float)q * scale + lo;
+}
+
+__global__ void quantize_pack_kernel(const void* src, int src_dtype, int64_t rows, int d, int bits,
+                                     bool k_order, uint8_t* codes, uint16_t* sl) {
+    extern __shared__ uint8_t qp_smem[];
+    const int warps = blockDim.x >> 5, wid = threadIdx.x >> 5;
+    const int64_t r = (int64_t)blockIdx.x * warps + wid;
+    if (r >= rows) return;
+    const int elem = src_dtype == DKV_F32 ? 4 : 2;
+    const int cb = bits == 16 ? d * elem : d * bits / 8;
+    quant_pack_vector(src, src_dtype, (size_t)r * d, d, bits, k_order, codes + r * cb,
+                      sl + r * (d / 64) * 2, src_dtype, qp_smem + wid * d);
+}
+
+// --------------------------------------------------------------------------
+// Drafter cache addressing.
+struct CompView {
+    uint8_t* k_codes;
+    uint8_t* v_codes;
+    uint16_t* k_sl;
+    uint16_t* v_sl;
+    int32_t* pos;
+    float* score;
+    int32_t* meta;
+    int32_t* seen;
+    int cap, cb_max, n_layers, n_kv, d;
+
+    DKV_DEV size_t bl(int b, int L) const { return (size_t)b * n_layers + L; }
+    DKV_DEV size_t vec(int b, int L, int h, int slot) const {
+        return ((bl(b, L) * n_kv + h) * (size_t)cap + slot);
+    }
+};
+
+struct FullView {
+    const void* k_pool;
+    const void* v_pool;
+    const int32_t* page_table;
+    int page_size, max_pages, dtype, n_layers, n_kv, d;
+
+    DKV_DEV size_t elem(int b, int L, int h, int p) const {
+        const int page = page_table[((size_t)b * n_layers + L) * max_pages + p / page_size];
+        return (((size_t)page * n_kv + h) * page_size + (p % page_size)) * (size_t)d;
+    }
+};
+
+struct LayerCfgs {
+    int n;
+    int bits[128];
+    int sink[128];
+    int recent[128];
+    double keep[128];
+};
+
+DKV_DEV int budget_of(double keep, int seen, int sink, int recent) {
+    const int s = seen > 1 ? seen : 1;
+    const int k = (int)rint(keep * (double)s);   // python round(): half to even
+    return k > sink + recent ? k : sink + recent;
+}
+
+// k-th smallest (0-based) of 64-bit keys over the slots that `pred` accepts,
+// by 8-bit radix passes.  All threads of the block call it.
+template <typename KeyFn>
+DKV_DEV unsigned long long block_select_kth(int hwm, int k, int key_bits, KeyFn key_of,
+                                            unsigned* hist, unsigned long long* shared_prefix,
+                                            int* shared_k) {
+    if (threadIdx.x == 0) {
+        *shared_prefix = 0ull;
+        *shared_k = k;
+    }
+    unsigned long long mask = 0ull;
+    for (int shift = key_bits - 8; shift >= 0; shift -= 8) {
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        const unsigned long long prefix = *shared_prefix;
+        for (int s = threadIdx.x; s < hwm; s += blockDim.x) {
+            unsigned long long key;
+            if (key_of(s, &key) && (key & mask) == prefix)
+                atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int kk = *shared_k;
+            unsigned cum = 0;
+            int bin = 0;
+            for (; bin < 256; ++bin) {
+                if (cum + hist[bin] > (unsigned)kk) break;
+                cum += hist[bin];
+            }
+            *shared_prefix = prefix | ((unsigned long long)bin << shift);
+            *shared_k = kk - (int)cum;
+        }
+        mask |= 255ull << shift;
+        __syncthreads();
+    }
+    return *shared_prefix;
+}
+
+// Finds the k-th (1-based) set bit of a 1024-bit map (32 words) with warp 0;
+// returns the bit index, or -1 when fewer than k bits are set.
+DKV_DEV int kth_set_bit(const uint32_t* bm, int k) {
+    const int lane = threadIdx.x & 31;
+    int c = __popc(bm[lane]);
+    int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (total < k) return -1;
+    const unsigned hit = __ballot_sync(0xffffffffu, incl >= k);
+    const int wl = __ffs(hit) - 1;
+    const int before = __shfl_sync(0xffffffffu, incl - c, wl);
+    int need = k - before;
+    uint32_t w = bm[wl];
+    int bit = -1;
+    for (int i = 0; i < 32; ++i) {
+        if ((w >> i) & 1u) {
+            if (--need == 0) {
+                bit = i;
+                break;
+            }
+        }
+    }
+    return wl * 32 + bit;
+}
+
+struct AppendArgs {
+    CompView c;
+    FullView f;
+    const void* src;
+    int src_dtype, rows_stride, src_rows_max, raw_dtype;
+    const int32_t* pos0;
+    const int32_t* n_rows;
+    const int32_t* trunc;
+    int advance_seen, layer0;
+    uint32_t* err;
+    LayerCfgs cfg;
+};
+
+constexpr int kAppendThreads = 512;
+constexpr int kAppendMaxRows = 1024;
+
+// One CTA per (layer, sequence): truncate, append + quantize, evict.
+__global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs a) {
+    extern __shared__ uint8_t ap_smem[];
+    __shared__ int slot_list[kAppendMaxRows];
+    __shared__ uint32_t bm_lo[32], bm_hi[32];
+    __shared__ __align__(16) unsigned hist[256];   // also read as 64-bit warp partials
+    __shared__ unsigned long long sh_prefix;
+    __shared__ int sh_k, sh_hwm, sh_found, sh_n, sh_pmax, sh_plo, sh_phi, sh_free;
+    __shared__ unsigned long long sh_min;
+    __shared__ int red_i[32];
+
+    const int li = blockIdx.x, b = blockIdx.y;
+    const int L = a.layer0 + li;
+    const CompView& c = a.c;
+    const int bits = a.cfg.bits[li], sink = a.cfg.sink[li], recent = a.cfg.recent[li];
+    const double keep = a.cfg.keep[li];
+    const size_t bl = c.bl(b, L);
+    int32_t* pos = c.pos + bl * c.cap;
+    float* score = c.score + bl * c.cap;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+
+    int hwm = c.meta[bl * 4 + 0];
+    const int trunc = a.trunc ? a.trunc[b] : -1;
+    if (trunc >= 0) {
+        for (int s = tid; s < hwm; s += blockDim.x)
+            if (pos[s] >= trunc) pos[s] = -1;
+    }
+    const int R = a.n_rows ? a.n_rows[b] : a.src_rows_max;
+    const int p0 = a.pos0 ? a.pos0[b] : 0;
+    if (R > kAppendMaxRows || R > a.src_rows_max) {
+        if (tid == 0) atomicOr(a.err, 0x10u);
+        return;
+    }
+    // seen: clipped by truncation, advanced to the last appended position + 1
+    int seen = c.seen[b];
+    if (trunc >= 0 && trunc < seen) seen = trunc;
+    if (a.advance_seen && R > 0 && p0 + R > seen) seen = p0 + R;
+    __syncthreads();
+
+    // ---- slots for the R new rows: lowest empty slots first, then extend hwm
+    if (tid == 0) {
+        sh_found = 0;
+        sh_hwm = hwm;
+    }
+    __syncthreads();
+    for (int base = 0; base < hwm; base += blockDim.x) {
+        if (sh_found >= R) break;
+        const int s = base + tid;
+        const bool empty = s < hwm && pos[s] < 0;
+        const unsigned ball = __ballot_sync(0xffffffffu, empty);
+        if (lane == 0) red_i[wid] = __popc(ball);
+        __syncthreads();
+        int before = sh_found;
+        for (int w = 0; w < wid; ++w) before += red_i[w];
+        const int idx = before + __popc(ball & ((1u << lane) - 1u));
+        if (empty && idx < R) slot_list[idx] = s;
+        __syncthreads();
+        if (tid == 0) {
+            int tot = 0;
+            for (int w = 0; w < nw; ++w) tot += red_i[w];
+            sh_found = min(R, sh_found + tot);
+        }
+        __syncthreads();
+    }
+    if (tid == 0) {
+        int f = sh_found;
+        int h2 = hwm;
+        while (f < R) slot_list[f++] = h2++;
+        sh_hwm = h2;
+    }
+    __syncthreads();
+    hwm = sh_hwm;
+    if (hwm > c.cap) {
+        if (tid == 0) atomicOr(a.err, 0x20u);
+        return;
+    }
+
+    // ---- quantize + pack the new rows (one warp per K or V vector)
+    const int d = c.d;
+    uint8_t* scratch = ap_smem + wid * d;
+    const int n_vec = R * c.n_kv * 2;
+    for (int v = wid; v < n_vec; v += nw) {
+        const int r = v / (2 * c.n_kv);
+        const int h = (v / 2) % c.n_kv;
+        const bool is_k = (v & 1) == 0;
+        const int slot = slot_list[r];
+        const size_t vi = c.vec(b, L, h, slot);
+        uint8_t* dst = (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max;
+        uint16_t* sl = (is_k ? c.k_sl : c.v_sl) + vi * (d / 64) * 2;
+        if (a.src) {
+            const size_t off = ((((size_t)b * a.rows_stride + r) * c.n_kv + h) * 2 + (is_k ? 0 : 1)) * d;
+            quant_pack_vector(a.src, a.src_dtype, off, d, bits, is_k, dst, sl, a.raw_dtype, scratch);
+        } else {
+            const size_t off = a.f.elem(b, L, h, p0 + r);
+            quant_pack_vector(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, off, d, bits, is_k, dst, sl,
+                              a.raw_dtype, scratch);
+        }
+    }
+    for (int r = tid; r < R; r += blockDim.x) {
+        pos[slot_list[r]] = p0 + r;
+        score[slot_list[r]] = 0.f;
+    }
+    __syncthreads();
+
+    if (R > 0) {
+        // ---- eviction (compress.py:159-179)
+        for (int i = tid; i < 32; i += blockDim.x) {
+            bm_lo[i] = 0;
+            bm_hi[i] = 0;
+        }
+        __syncthreads();
+        int n_loc = 0, pmax_loc = -1;
+        for (int s = tid; s < hwm; s += blockDim.x) {
+            const int p = pos[s];
+            if (p >= 0) {
+                ++n_loc;
+                pmax_loc = max(pmax_loc, p);
+                if (p < 1024) atomicOr(&bm_lo[p >> 5], 1u << (p & 31));
+            }
+        }
+        n_loc = warp_sum_i(n_loc);
+        pmax_loc = warp_max_i(pmax_loc);
+        if (lane == 0) red_i[wid] = n_loc;
+        __syncthreads();
+        if (tid == 0) {
+            int t = 0;
+            for (int w = 0; w < nw; ++w) t += red_i[w];
+            sh_n = t;
+        }
+        __syncthreads();
+        if (lane == 0) red_i[wid] = pmax_loc;
+        __syncthreads();
+        if (tid == 0) {
+            int t = -1;
+            for (int w = 0; w < nw; ++w) t = max(t, red_i[w]);
+            sh_pmax = t;
+        }
+        __syncthreads();
+        const int n = sh_n, pmax = sh_pmax;
+        const int budget = budget_of(keep, seen, sink, recent);
+        bool do_evict = n > budget && recent > 0 && recent < n;
+        if (do_evict) {
+            // sink-th lowest position
+            if (wid == 0) {
+                int plo = -1;
+                if (sink > 0) {
+                    plo = kth_set_bit(bm_lo, sink);
+                    if (plo < 0) plo = -2;   // fall back to a radix select
+                }
+                if (lane == 0) sh_plo = plo;
+            }
+            // recent-th highest position, from a window below pmax
+            for (int s = tid; s < hwm; s += blockDim.x) {
+                const int p = pos[s];
+                if (p >= 0 && pmax - p < 1024) atomicOr(&bm_hi[(pmax - p) >> 5], 1u << ((pmax - p) & 31));
+            }
+            __syncthreads();
+            if (wid == 0) {
+                int o = kth_set_bit(bm_hi, recent);
+                if (lane == 0) sh_phi = o < 0 ? -2 : pmax - o;
+            }
+            __syncthreads();
+            if (sh_plo == -2) {
+                auto key = [&](int s, unsigned long long* k) {
+                    const int p = pos[s];
+                    *k = (unsigned long long)(uint32_t)p;
+                    return p >= 0;
+                };
+                unsigned long long v = block_select_kth(hwm, sink - 1, 32, key, hist, &sh_prefix, &sh_k);
+                if (tid == 0) sh_plo = (int)v;
+                __syncthreads();
+            }
+            if (sh_phi == -2) {
+                auto key = [&](int s, unsigned long long* k) {
+                    const int p = pos[s];
+                    *k = (unsigned long long)(uint32_t)p;
+                    return p >= 0;
+                };
+                unsigned long long v = block_select_kth(hwm, n - recent, 32, key, hist, &sh_prefix, &sh_k);
+                if (tid == 0) sh_phi = (int)v;
+                __syncthreads();
+            }
+            const int plo = sh_plo, phi = sh_phi;
+            int fr = 0;
+            for (int s = tid; s < hwm; s += blockDim.x) {
+                const int p = pos[s];
+                fr += (p > plo && p < phi) ? 1 : 0;
+            }
+            fr = warp_sum_i(fr);
+            __syncthreads();
+            if (lane == 0) red_i[wid] = fr;
+            __syncthreads();
+            if (tid == 0) {
+                int t = 0;
+                for (int w = 0; w < nw; ++w) t += red_i[w];
+                sh_free = t;
+            }
+            __syncthreads();
+            const int drop = min(n - budget, sh_free);
+            auto free_key = [&](int s, unsigned long long* k) {
+                const int p = pos[s];
+                *k = ((unsigned long long)__float_as_uint(score[s]) << 32) | (uint32_t)p;
+                return p > plo && p < phi;
+            };
+            if (drop > 0 && drop <= 8) {
+                for (int it = 0; it < drop; ++it) {
+                    unsigned long long best = ~0ull;
+                    for (int s = tid; s < hwm; s += blockDim.x) {
+                        unsigned long long k;
+                        if (free_key(s, &k) && k < best) best = k;
+                    }
+                    best = warp_min_u64(best);
+                    __syncthreads();
+                    if (lane == 0) reinterpret_cast<unsigned long long*>(hist)[wid] = best;
+                    __syncthreads();
+                    if (tid == 0) {
+                        unsigned long long m = ~0ull;
+                        for (int w = 0; w < nw; ++w) {
+                            unsigned long long t = reinterpret_cast<unsigned long long*>(hist)[w];
+                            m = t < m ? t : m;
+                        }
+                        sh_min = m;
+                    }
+                    __syncthreads();
+                    const unsigned long long m = sh_min;
+                    for (int s = tid; s < hwm; s += blockDim.x) {
+                        unsigned long long k;
+                        if (free_key(s, &k) && k == m) pos[s] = -1;
+                    }
+                    __syncthreads();
+                }
+            } else if (drop > 8) {
+                const unsigned long long thr = block_select_kth(hwm, drop - 1, 64, free_key, hist, &sh_prefix, &sh_k);
+                __syncthreads();
+                for (int s = tid; s < hwm; s += blockDim.x) {
+                    unsigned long long k;
+                    if (free_key(s, &k) && k <= thr) pos[s] = -1;
+                }
+                __syncthreads();
+            }
+        }
+    }
+    // ---- shrink hwm to the last live slot, recount
+    __syncthreads();
+    int last = -1, cnt = 0;
+    for (int s = tid; s < hwm; s += blockDim.x)
+        if (pos[s] >= 0) {
+            last = max(last, s);
+            ++cnt;
+        }
+    last = warp_max_i(last);
+    cnt = warp_sum_i(cnt);
+    __syncthreads();
+    if (lane == 0) {
+        red_i[wid] = last;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int t = -1;
+        for (int w = 0; w < nw; ++w) t = max(t, red_i[w]);
+        sh_hwm = t + 1;
+    }
+    __syncthreads();
+    if (lane == 0) red_i[wid] = cnt;
+    __syncthreads();
+    if (tid == 0) {
+        int t = 0;
+        for (int w = 0; w < nw; ++w) t += red_i[w];
+        c.meta[bl * 4 + 0] = sh_hwm;
+        c.meta[bl * 4 + 1] = t;
+        if (L == 0 && a.advance_seen) c.seen[b] = seen;
+        else if (L == 0 && trunc >= 0) c.seen[b] = seen;
+    }
+}
+
+// Rebuild: clear the layer and refill it from the full cache with the rows
+// that survive eviction when every score is zero (sink rows + newest rows).
+struct RebuildArgs {
+    CompView c;
+    FullView f;
+    const int32_t* ctx;
+    uint32_t* err;
+    int raw_dtype, advance_seen, rows_per_cta;
+    int layer_ids[128];
+    LayerCfgs cfg;
+};
+
+DKV_DEV void rebuild_plan(const RebuildArgs& a, int li, int b, int* kept, int* gap_at, int* gap_len,
+                          int* seen_out) {
+    const int n = a.ctx[b];
+    int seen = a.c.seen[b];
+    if (a.advance_seen && n > seen) seen = n;
+    const int sink = a.cfg.sink[li], recent = a.cfg.recent[li];
+    const int budget = budget_of(a.cfg.keep[li], seen, sink, recent);
+    *seen_out = seen;
+    if (n <= budget || recent <= 0) {
+        *kept = n;
+        *gap_at = n;
+        *gap_len = 0;
+        return;
+    }
+    const int s0 = min(sink, n);
+    const int n_drop = n - budget;
+    *kept = n - n_drop;
+    *gap_at = s0;
+    *gap_len = n_drop;
+}
+
+__global__ void comp_rebuild_kernel(RebuildArgs a) {
+    extern __shared__ uint8_t rb_smem[];
+    const int li = blockIdx.y, b = blockIdx.z;
+    const int L = a.layer_ids[li];
+    const CompView& c = a.c;
+    int kept, gap_at, gap_len, seen;
+    rebuild_plan(a, li, b, &kept, &gap_at, &gap_len, &seen);
+    const size_t bl = c.bl(b, L);
+    const int bits = a.cfg.bits[li];
+    if (kept > c.cap) {   // the caller sized the slot array too small: report, write nothing
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.err, 0x20u);
+        return;
+    }
+    // every chunk of [0, cap) is visited: live slots get their position,
+    // the rest are cleared (no CTA depends on the old high-water mark)
+    const int r0 = blockIdx.x * a.rows_per_cta;
+    if (r0 >= c.cap) return;
+    const int r1 = min(r0 + a.rows_per_cta, c.cap);
+    const int wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int s = r0 + threadIdx.x; s < r1; s += blockDim.x) {
+        if (s < kept) {
+            c.pos[bl * c.cap + s] = s < gap_at ? s : s + gap_len;
+            c.score[bl * c.cap + s] = 0.f;
+        } else {
+            c.pos[bl * c.cap + s] = -1;
+        }
+    }
+    const int d = c.d;
+    const int rq1 = min(r1, kept);
+    const int n_vec = (rq1 > r0 ? rq1 - r0 : 0) * c.n_kv * 2;
+    uint8_t* scratch = rb_smem + wid * d;
+    for (int v = wid; v < n_vec; v += nw) {
+        const int s = r0 + v / (2 * c.n_kv);
+        const int h = (v / 2) % c.n_kv;
+        const bool is_k = (v & 1) == 0;
+        const int p = s < gap_at ? s : s + gap_len;
+        const size_t vi = c.vec(b, L, h, s);
+        quant_pack_vector(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, a.f.elem(b, L, h, p), d, bits, is_k,
+                          (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max,
+                          (is_k ? c.k_sl : c.v_sl) + vi * (d / 64) * 2, a.raw_dtype, scratch);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        c.meta[bl * 4 + 0] = kept;
+        c.meta[bl * 4 + 1] = kept;
+    }
+}
+
+// seen update after a rebuild (one thread per sequence)
+__global__ void comp_seen_kernel(int32_t* seen, const int32_t* ctx, int batch, int advance, int trunc_zero) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= batch) return;
+    int s = seen[b];
+    if (trunc_zero) s = 0;
+    if (advance && ctx[b] > s) s = ctx[b];
+    seen[b] = s;
+}
+
+// Read-back (tests): every slot of [0, n_slots) in slot order, dequantized,
+// with its position (-1 = empty) and score; the caller sorts by position.
+__global__ void comp_read_kernel(CompView c, int b, int L, int bits, int raw_dtype, int n_slots,
+                                 float* k, float* v, int32_t* pos_out, float* score_out) {
+    const int slot = blockIdx.x;
+    if (slot >= n_slots) return;
+    const size_t bl = c.bl(b, L);
+    const int p = c.pos[bl * c.cap + slot];
+    if (threadIdx.x == 0) {
+        pos_out[slot] = p;
+        if (score_out) score_out[slot] = c.score[bl * c.cap + slot];
+    }
+    const int d = c.d;
+    for (int t = threadIdx.x; t < c.n_kv * d; t += blockDim.x) {
+        const int h = t / d, e = t % d;
+        const size_t vi = c.vec(b, L, h, slot);
+        float kv = 0.f, vv = 0.f;
+        if (p >= 0) {
+            kv = dequant_elem(c.k_codes + vi * c.cb_max, c.k_sl + vi * (d / 64) * 2, d, bits, true, e, raw_dtype);
+            vv = dequant_elem(c.v_codes + vi * c.cb_max, c.v_sl + vi * (d / 64) * 2, d, bits, false, e, raw_dtype);
+        }
+        k[((size_t)slot * c.n_kv + h) * d + e] = kv;
+        v[((size_t)slot * c.n_kv + h) * d + e] = vv;
+    }
+}
+
+// ------------------------------------------------------------------ full cache
+__global__ void full_write_kernel(FullView f, int L, const void* src, int rows, const int32_t* pos0,
+                                  const int32_t* n_rows) {
+    const int b = blockIdx.y, r = blockIdx.x;
+    const int nr = n_rows ? n_rows[b] : rows;
+    if (r >= nr) return;
+    const int p = pos0[b] + r;
+    for (int t = threadIdx.x; t < f.n_kv * f.d * 2; t += blockDim.x) {
+        const int kv = t / (f.n_kv * f.d);
+        const int h = (t / f.d) % f.n_kv, e = t % f.d;
+        const size_t si = ((((size_t)b * rows + r) * f.n_kv + h) * 2 + kv) * f.d + e;
+        const float val = load_as_f32(src, f.dtype, si);
+        store_from_f32(const_cast<void*>(kv ? f.v_pool : f.k_pool), f.dtype, f.elem(b, L, h, p) + e, val);
+    }
+}
+
+__global__ void full_read_kernel(FullView f, int b, int L, int n, void* dst) {
+    const int r = blockIdx.x;
+    if (r >= n) return;
+    for (int t = threadIdx.x; t < f.n_kv * f.d * 2; t += blockDim.x) {
+        const int kv = t / (f.n_kv * f.d);
+        const int h = (t / f.d) % f.n_kv, e = t % f.d;
+        const float val = load_as_f32(kv ? f.v_pool : f.k_pool, f.dtype, f.elem(b, L, h, r) + e);
+        store_from_f32(dst, f.dtype, (((size_t)r * f.n_kv + h) * 2 + kv) * f.d + e, val);
+    }
+}
+
+// --------------------------------------------------------------------------
+// host side
+CompView comp_view(const dkv_comp_cache* c, dkv_dims dims) {
+    CompView v;
+    v.k_codes = c->k_codes;
+    v.v_codes = c->v_codes;
+    v.k_sl = c->k_sl;
+    v.v_sl = c->v_sl;
+    v.pos = c->pos;
+    v.score = c->score;
+    v.meta = c->meta;
+    v.seen = c->seen;
+    v.cap = c->cap;
+    v.cb_max = c->cb_max;
+    v.n_layers = dims.n_layers;
+    v.n_kv = dims.n_kv;
+    v.d = dims.d;
+    return v;
+}
+
+FullView full_view(const dkv_full_cache* f, dkv_dims dims) {
+    FullView v;
+    v.k_pool = f ? f->k_pool : nullptr;
+    v.v_pool = f ? f->v_pool : nullptr;
+    v.page_table = f ? f->page_table : nullptr;
+    v.page_size = f ? f->page_size : 16;
+    v.max_pages = f ? f->max_pages : 0;
+    v.dtype = f ? f->dtype : DKV_BF16;
+    v.n_layers = dims.n_layers;
+    v.n_kv = dims.n_kv;
+    v.d = dims.d;
+    return v;
+}
+
+uint32_t* device_error_word();
+
+}  // namespace dkv
+
+using namespace dkv;
+
+extern "C" int dkv_quantize(const float* x, int64_t rows, int d, int bits, uint8_t* codes,
+                            float* scale, float* lo, float* deq, void* stream) {
+    DKV_REQUIRE(x != nullptr && rows >= 0 && d > 0, "dkv_quantize: bad arguments");
+    DKV_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 8 || bits == 16,
+                "dkv_quantize: unsupported bits=%d", bits);
+    if (rows == 0) return DKV_OK;
+    const int ng = (d + 63) / 64;
+    const int64_t warps = rows * ng;
+    const int threads = 256;
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    quantize_exact_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(x, rows, d, bits, codes,
+                                                                                  scale, lo, deq);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+
+extern "C" int dkv_quantize_pack(const void* src, int src_dtype, int64_t rows, int d, int bits,
+                                 int k_order, uint8_t* codes, uint16_t* sl, void* stream) {
+    DKV_REQUIRE(src && codes && sl && rows >= 0, "dkv_quantize_pack: bad arguments");
+    DKV_REQUIRE(d % 64 == 0 && d <= 256, "dkv_quantize_pack: d must be 64, 128 or 256 (got %d)", d);
+    DKV_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 8 || bits == 16, "bad bits %d", bits);
+    if (rows == 0) return DKV_OK;
+    const int warps = 8;
+    quantize_pack_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, warps * d,
+                           (cudaStream_t)stream>>>(src, src_dtype, rows, d, bits, k_order != 0, codes, sl);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+
+static int fill_cfgs(const dkv_comp_cache* c, const int32_t* layers, int n_sel, int layer0, int d, int raw_elem,
+                     LayerCfgs* out) {
+    DKV_REQUIRE(n_sel > 0 && n_sel <= 128, "at most 128 layers per call (got %d)", n_sel);
+    DKV_REQUIRE(c->bits && c->keep && c->sink && c->recent, "per-layer config arrays are required");
+    out->n = n_sel;
+    for (int i = 0; i < n_sel; ++i) {
+        const int L = layers ? layers[i] : layer0 + i;
+        const int bits = c->bits[L];
+        DKV_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 8 || bits == 16, "layer %d: bits %d", L, bits);
+        const int cb = bits == 16 ? d * raw_elem : d * bits / 8;
+        DKV_REQUIRE(cb <= c->cb_max, "layer %d: %d-bit vectors need %d bytes > cb_max %d", L, bits, cb, c->cb_max);
+        DKV_REQUIRE(c->keep[L] > 0.0 && c->keep[L] <= 1.0, "layer %d: keep %f", L, c->keep[L]);
+        DKV_REQUIRE(c->sink[L] >= 0 && c->recent[L] >= 0, "layer %d: sink/recent", L);
+        out->bits[i] = bits;
+        out->keep[i] = c->keep[L];
+        out->sink[i] = c->sink[L];
+        out->recent[i] = c->recent[L];
+    }
+    return DKV_OK;
+}
+
+static int check_comp(const dkv_comp_cache* c, dkv_dims dims, int raw_elem) {
+    DKV_REQUIRE(c && c->k_codes && c->v_codes && c->k_sl && c->v_sl && c->pos && c->score && c->meta &&
+                    c->seen,
+                "drafter cache pointers must be set");
+    DKV_REQUIRE(dims.d % 64 == 0 && dims.d <= 256, "head dim %d unsupported (64/128/256)", dims.d);
+    DKV_REQUIRE(c->cb_max >= dims.d * raw_elem || c->cb_max >= dims.d, "cb_max too small");
+    DKV_REQUIRE(c->cap > 0, "cap must be positive");
+    return DKV_OK;
+}
+
+extern "C" int dkv_comp_append(const dkv_comp_cache* comp, const dkv_full_cache* full, dkv_dims dims,
+                               int layer0, int n_layer_sel, const void* src, int src_dtype, int rows_stride,
+                               const int32_t* pos0, const int32_t* n_rows, const int32_t* trunc,
+                               int advance_seen, void* stream) {
+    const int raw_dtype = full ? full->dtype : src_dtype;
+    DKV_TRY(check_comp(comp, dims, raw_dtype == DKV_F32 ? 4 : 2));
+    DKV_REQUIRE(layer0 >= 0 && layer0 + n_layer_sel <= dims.n_layers, "layer range");
+    DKV_REQUIRE(rows_stride >= 0 && rows_stride <= kAppendMaxRows, "rows_stride %d > %d", rows_stride,
+                kAppendMaxRows);
+    DKV_REQUIRE(rows_stride == 0 || src != nullptr || (full && full->k_pool && full->page_table),
+                "dkv_comp_append: rows to append but no row source");
+    AppendArgs a;
+    a.c = comp_view(comp, dims);
+    a.f = full_view(full, dims);
+    a.src = src;
+    a.src_dtype = src_dtype;
+    a.rows_stride = rows_stride;
+    a.src_rows_max = rows_stride;
+    a.raw_dtype = raw_dtype;
+    a.pos0 = pos0;
+    a.n_rows = n_rows;
+    a.trunc = trunc;
+    a.advance_seen = advance_seen;
+    a.layer0 = layer0;
+    a.err = device_error_word();
+    DKV_TRY(fill_cfgs(comp, nullptr, n_layer_sel, layer0, dims.d, raw_dtype == DKV_F32 ? 4 : 2, &a.cfg));
+    const size_t smem = (kAppendThreads / 32) * dims.d;
+    dim3 grid(n_layer_sel, dims.batch);
+    comp_append_kernel<<<grid, kAppendThreads, smem, (cudaStream_t)stream>>>(a);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+
+extern "C" int dkv_comp_rebuild(const dkv_comp_cache* comp, const dkv_full_cache* full, dkv_dims dims,
+                                const int32_t* layers, int n_sel, const int32_t* ctx, int advance_seen,
+                                void* stream) {
+    DKV_REQUIRE(full && full->k_pool && full->page_table, "rebuild needs the full cache");
+    DKV_TRY(check_comp(comp, dims, full->dtype == DKV_F32 ? 4 : 2));
+    DKV_REQUIRE(layers && ctx, "layers / ctx required");
+    RebuildArgs a;
+    a.c = comp_view(comp, dims);
+    a.f = full_view(full, dims);
+    a.ctx = ctx;
+    a.err = device_error_word();
+    a.raw_dtype = full->dtype;
+    a.advance_seen = advance_seen;
+    a.rows_per_cta = 64;
+    DKV_TRY(fill_cfgs(comp, layers, n_sel, 0, dims.d, full->dtype == DKV_F32 ? 4 : 2, &a.cfg));
+    for (int i = 0; i < n_sel; ++i) {
+        DKV_REQUIRE(layers[i] >= 0 && layers[i] < dims.n_layers, "layer id %d", layers[i]);
+        a.layer_ids[i] = layers[i];
+    }
+    const int warps = 8;
+    dim3 grid((comp->cap + a.rows_per_cta - 1) / a.rows_per_cta, n_sel, dims.batch);
+    comp_rebuild_kernel<<<grid, warps * 32, warps * dims.d, (cudaStream_t)stream>>>(a);
+    DKV_LAUNCHED();
+    // the layer-0 rebuild advances `seen` (compress.py:131-132); done after all
+    // CTAs read it, in stream order
+    bool has0 = false;
+    for (int i = 0; i < n_sel; ++i) has0 |= layers[i] == 0;
+    if (has0 && advance_seen) {
+        comp_seen_kernel<<<(dims.batch + 127) / 128, 128, 0, (cudaStream_t)stream>>>(comp->seen, ctx, dims.batch,
+                                                                                     1, 0);
+        DKV_LAUNCHED();
+    }
+    return DKV_OK;
+}
+
+extern "C" int dkv_comp_read(const dkv_comp_cache* comp, dkv_dims dims, int b, int layer, int max_n,
+                             float* k, float* v, int32_t* pos, float* score, int* n_out, void* stream) {
+    DKV_REQUIRE(comp && k && v && pos && n_out && comp->bits, "dkv_comp_read: bad arguments");
+    DKV_REQUIRE(b >= 0 && b < dims.batch && layer >= 0 && layer < dims.n_layers, "dkv_comp_read: index");
+    cudaStream_t st = (cudaStream_t)stream;
+    const size_t bl = (size_t)b * dims.n_layers + layer;
+    int meta[4];
+    DKV_CUDA(cudaMemcpyAsync(meta, comp->meta + bl * 4, sizeof(meta), cudaMemcpyDeviceToHost, st));
+    DKV_CUDA(cudaStreamSynchronize(st));
+    const int hwm = meta[0];
+    *n_out = hwm;
+    DKV_REQUIRE(hwm <= max_n, "dkv_comp_read: %d slots > max_n %d", hwm, max_n);
+    if (hwm == 0) return DKV_OK;
+    const int raw_dtype = comp->cb_max >= dims.d * 4 ? DKV_F32 : DKV_BF16;
+    comp_read_kernel<<<hwm, 256, 0, st>>>(comp_view(comp, dims), b, layer, comp->bits[layer], raw_dtype, hwm, k,
+                                          v, pos, score);
+    DKV_LAUNCHED();
+    DKV_CUDA(cudaStreamSynchronize(st));
+    return DKV_OK;
+}
+
+extern "C" int dkv_full_write(const dkv_full_cache* full, dkv_dims dims, int layer, const void* src, int rows,
+                              const int32_t* pos0, const int32_t* n_rows, void* stream) {
+    DKV_REQUIRE(full && full->k_pool && full->v_pool && full->page_table && src && pos0, "dkv_full_write args");
+    DKV_REQUIRE(layer >= 0 && layer < dims.n_layers && rows >= 0, "dkv_full_write: layer/rows");
+    if (rows == 0) return DKV_OK;
+    FullView f = full_view(full, dims);
+    full_write_kernel<<<dim3(rows, dims.batch), 256, 0, (cudaStream_t)stream>>>(f, layer, src, rows, pos0, n_rows);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+
+extern "C" int dkv_full_read(const dkv_full_cache* full, dkv_dims dims, int b, int layer, int n, void* dst,
+                             void* stream) {
+    DKV_REQUIRE(full && full->k_pool && dst && n >= 0, "dkv_full_read args");
+    if (n == 0) return DKV_OK;
+    FullView f = full_view(full, dims);
+    full_read_kernel<<<n, 256, 0, (cudaStream_t)stream>>>(f, b, layer, n, dst);
+    DKV_LAUNCHED();
+    return DKV_OK;
+}

@@ -106,10 +106,11 @@ def _unpack_lanes(b: np.ndarray, bits: int, n: int) -> np.ndarray:
     return out.reshape(rows, n)
 
 
-def pack_codes(codes: np.ndarray, bits: int) -> np.ndarray:
-    """codes [rows, d] in element order -> packed bytes [rows, d*bits/8]."""
+def pack_codes(codes: np.ndarray, bits: int, k_order: bool = True) -> np.ndarray:
+    """codes [rows, d] in element order -> packed bytes [rows, d*bits/8].
+    K vectors use the fragment order, V vectors (k_order=False) element order."""
     rows, d = codes.shape
-    s = codes[:, fragment_order(d)].astype(np.uint32)      # storage order
+    s = codes[:, fragment_order(d) if k_order else np.arange(d)].astype(np.uint32)   # storage order
     if bits == 8:
         return s.astype(np.uint8)
     if bits in (2, 4):

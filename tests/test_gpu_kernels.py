@@ -1,0 +1,281 @@
+"""Kernel-level parity on the GPU, through the C ABI, against the CPU oracle.
+
+Bit-exact where the work is integer / byte / index work (quantization codes,
+scales, packed bytes, kept slot sets); within an fp32 tolerance written in each
+test for floating point.
+"""
+
+import ctypes as C
+import json
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle.caches import OracleComp
+from draftkv.config import CompressionConfig
+from draftkv.weights import round_bf16
+from tests.golden.make_golden import QUANT_CASES
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def lib():
+    from draftkv import _lib
+    return _lib
+
+
+@pytest.fixture(scope="module")
+def quant_npz(golden_dir):
+    return np.load(golden_dir / "quantize.npz")
+
+
+# ------------------------------------------------------------------ K1
+@pytest.mark.parametrize("cid", [c for _, c in QUANT_CASES])
+@pytest.mark.parametrize("bits", [2, 3, 4, 8, 16])
+def test_quantize_matches_reference_bit_for_bit(quant_npz, cid, bits):
+    from draftkv import quantize
+    x = quant_npz[f"x{cid}"]
+    got = quantize(x, bits)
+    want = quant_npz[f"deq{cid}_b{bits}"]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+def test_codes_scale_lo_bit_exact(bits):
+    from draftkv import quantize_codes
+    rng = np.random.default_rng(bits)
+    x = (rng.standard_normal((300, 2, 128)) * rng.uniform(0.1, 30.0, (300, 2, 1))).astype(np.float32)
+    x[3] = 0.5        # constant vectors: scale clamps to 1e-8
+    codes, scale, lo, deq = quantize_codes(x, bits)
+    rc, rs, rl, rd = oracle.quant_codes(x, bits)
+    assert np.array_equal(codes, rc)
+    assert np.array_equal(scale.view(np.uint32), rs.view(np.uint32))
+    assert np.array_equal(lo.view(np.uint32), rl.view(np.uint32))
+    assert np.array_equal(deq.view(np.uint32), rd.view(np.uint32))
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("k_order", [1, 0])
+@pytest.mark.parametrize("src_dtype", ["f32", "bf16"])
+def test_packed_storage_bytes(d, bits, k_order, src_dtype):
+    L = lib()
+    rng = np.random.default_rng(d * 10 + bits)
+    x = round_bf16(rng.standard_normal((97, d)).astype(np.float32) * 3)
+    tdt = torch.float32 if src_dtype == "f32" else torch.bfloat16
+    src = torch.from_numpy(x).to("cuda", tdt)
+    codes = torch.zeros((97, d * bits // 8), dtype=torch.uint8, device="cuda")
+    sl = torch.zeros((97, d // 64, 2), dtype=torch.int16, device="cuda")
+    L.call("dkv_quantize_pack", src.data_ptr(), L.F32 if src_dtype == "f32" else L.BF16, 97, d, bits, k_order,
+           codes.data_ptr(), sl.data_ptr(), L.stream_ptr())
+    rc, rs, rl, _ = oracle.quant_codes(x, bits)
+    want = oracle.pack_codes(rc[:, :d], bits, k_order=bool(k_order))
+    assert np.array_equal(codes.cpu().numpy(), want)
+    got_sl = sl.cpu().numpy().view(np.float16)
+    assert np.array_equal(got_sl[:, :, 0], rs.astype(np.float16))
+    assert np.array_equal(got_sl[:, :, 1], rl.astype(np.float16))
+
+
+# ------------------------------------------------------------- K6 / K7
+def _dev_comp(cfg, n_layers=2, n_kv=2, d=64, cap=64):
+    from draftkv import CompressedKVCache
+    return CompressedKVCache(n_layers, cfg, n_kv=n_kv, d_head=d, dtype=np.float32, capacity=cap)
+
+
+def test_eviction_trace_matches_reference(golden_dir):
+    """Replays the reference trace (append + note_attention, truncation) on the
+    device cache: kept positions exact after every step, scores to fp32."""
+    states = json.loads((golden_dir / "evict_trace.json").read_text())["states"]
+    comp = _dev_comp(CompressionConfig(bits=4, keep_frac=0.5, sink=2, recent=4))
+    rng = np.random.default_rng(7)
+    pos = 0
+    for step, want in enumerate(states):
+        n_rows = 1 if step % 7 else 3
+        for L in range(2):
+            k = rng.standard_normal((n_rows, 2, 64)).astype(np.float32)
+            v = rng.standard_normal((n_rows, 2, 64)).astype(np.float32)
+            comp.append(L, k, v, np.arange(pos, pos + n_rows))
+            n_live = len(comp.read(L)[2])
+            probs = rng.random((1, 2, n_live)).astype(np.float32)
+            probs /= probs.sum(-1, keepdims=True)
+            comp.note_attention(L, probs)
+        pos += n_rows
+        if step % 9 == 8:
+            pos -= 2
+            comp.truncate(pos)
+        assert comp.seen_positions == want["seen"], step
+        for L in range(2):
+            p, s = comp.scores(L)
+            assert p.tolist() == want["pos"][L], (step, L)
+            np.testing.assert_allclose(s, want["score"][L], rtol=2e-6, atol=1e-6)
+
+
+def _filled_full(n, n_layers=2, n_kv=2, d=64, seed=0, dtype=np.float32):
+    from draftkv import FullKVCache
+    full = FullKVCache(n_layers, n_kv, d, dtype, capacity=max(n, 16))
+    ref = oracle.OracleFull(n_layers)
+    rng = np.random.default_rng(seed)
+    for L in range(n_layers):
+        k = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+        v = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+        full.append(L, k, v, np.arange(n))
+        ref.append(L, k, v, np.arange(n))
+    return full, ref
+
+
+@pytest.mark.parametrize("cfg", [CompressionConfig(4, 0.5), CompressionConfig(2, 0.25, 4, 8),
+                                 CompressionConfig(8, 1.0), CompressionConfig(3, 0.5, 0, 16),
+                                 CompressionConfig(16, 0.25)], ids=lambda c: c.label() + f"-s{c.sink}r{c.recent}")
+def test_sync_from_zero_keeps_the_reference_slots(cfg):
+    full, ref = _filled_full(150)
+    comp = _dev_comp(cfg, cap=256)
+    rcomp = OracleComp(2, cfg)
+    assert comp.sync_from(full, 0) == rcomp.sync_from(ref, 0)
+    assert comp.seen_positions == rcomp.seen
+    for L in range(2):
+        k, v, p = comp.read(L)
+        assert p.tolist() == rcomp.pos[L]
+        rk = np.stack(rcomp.k[L])
+        rv = np.stack(rcomp.v[L])
+        # fp16 storage of (scale, lo) against the reference's fp32: half a step
+        tol = 0.51 * (np.abs(rk).max() / ((1 << cfg.bits) - 1) if cfg.bits < 16 else 1e-6) + 1e-3
+        assert np.abs(k - rk).max() <= tol
+        assert np.abs(v - rv).max() <= 0.51 * (np.abs(rv).max() / ((1 << cfg.bits) - 1) if cfg.bits < 16 else 1e-6) + 1e-3
+
+
+def test_resync_rewrites_the_suffix():
+    """Reference tests/test_lossless.py:60-77 on the device cache."""
+    full, ref = _filled_full(120)
+    comp = _dev_comp(CompressionConfig(8, 1.0), cap=256)
+    comp.sync_from(full, 0)
+    assert comp.length == full.length
+    comp.truncate(10)
+    assert comp.length == 10
+    rows = comp.sync_from(full, 10)
+    assert rows == (120 - 10) * 2
+    assert comp.length == 120
+
+
+def test_resync_with_eviction_matches_reference():
+    cfg = CompressionConfig(4, 0.5, 2, 6)
+    full, ref = _filled_full(80)
+    comp = _dev_comp(cfg, cap=128)
+    rcomp = OracleComp(2, cfg)
+    comp.sync_from(full, 0)
+    rcomp.sync_from(ref, 0)
+    rng = np.random.default_rng(3)
+    for it in range(6):
+        for L in range(2):
+            n = len(rcomp.pos[L])
+            probs = rng.random((1, 2, n)).astype(np.float32)
+            comp.note_attention(L, probs)
+            rcomp.note_attention(L, probs)
+        cut = 80 - 3 * (it + 1)
+        comp.truncate(cut)
+        rcomp.truncate(cut)
+        assert comp.sync_from(full, cut) == rcomp.sync_from(ref, cut)
+        for L in range(2):
+            assert comp.read(L)[2].tolist() == rcomp.pos[L], (it, L)
+
+
+def test_only_changed_layers_are_rebuilt():
+    """Reference tests/test_adaptive.py:130-153 on the device cache."""
+    full, _ = _filled_full(64, n_layers=3)
+    a, b = CompressionConfig(2, 0.25), CompressionConfig(8, 1.0)
+    comp = _dev_comp([a, a, a], n_layers=3, cap=128)
+    comp.sync_from(full, 0)
+    before = [comp.read(L)[0].copy() for L in range(3)]
+    rows = comp.rebuild_layers(full, [1], [a, b, a])
+    assert rows == 64 and comp.cfgs[1] == b
+    for L in range(3):
+        same = comp.read(L)[0].shape == before[L].shape and np.array_equal(comp.read(L)[0], before[L])
+        assert same == (L != 1), L
+
+
+# ------------------------------------------------------------------- K4
+def _gemm(x, w_tiled, M, N, K, kind, dtype_code, out=None, ld=None, work=None):
+    L = lib()
+    if work is None:
+        work = torch.zeros(int(L.load().dkv_gemm_work_bytes(M, N, K, dtype_code)), dtype=torch.uint8, device="cuda")
+    e = L.EpilogueS()
+    e.kind = kind
+    e.out_f32 = out.data_ptr()
+    e.ld_out = ld
+    e.act_dtype = dtype_code
+    L.call("dkv_gemm", x.data_ptr(), dtype_code, w_tiled.data_ptr(), dtype_code, M, N, K, C.byref(e),
+           work.data_ptr(), work.numel(), L.stream_ptr())
+    return work
+
+
+@pytest.mark.parametrize("M,K", [(256, 128), (384, 576), (1024, 1536)])
+def test_bf16_gemm_matches_torch_and_is_batch_invariant(M, K):
+    L = lib()
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    W = (torch.randn((M, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    Wt = torch.empty_like(W)
+    L.call("dkv_pack_weight", W.data_ptr(), M, K, Wt.data_ptr(), L.stream_ptr())
+    X = torch.randn((100, K), generator=g, device="cuda").to(torch.bfloat16)
+    ref = X.float() @ W.float().t()
+    outs = {}
+    for N in (1, 5, 37, 64, 100):
+        out = torch.zeros((N, M), dtype=torch.float32, device="cuda")
+        _gemm(X[:N].contiguous(), Wt, M, N, K, L.EPI_STORE, L.BF16, out=out, ld=M)
+        torch.testing.assert_close(out, ref[:N], rtol=1e-4, atol=1e-4)
+        outs[N] = out
+    for N in (5, 37, 64, 100):     # token 0's column is bit-identical whatever N
+        assert torch.equal(outs[N][0], outs[1][0])
+    assert torch.equal(outs[100][:64], outs[64])
+
+
+def test_f32_gemm_matches_torch():
+    L = lib()
+    M, K = 256, 192
+    g = torch.Generator(device="cuda").manual_seed(1)
+    W = torch.randn((M, K), generator=g, device="cuda")
+    X = torch.randn((9, K), generator=g, device="cuda")
+    out = torch.zeros((9, M), device="cuda")
+    _gemm(X, W, M, 9, K, L.EPI_STORE, L.F32, out=out, ld=M)
+    torch.testing.assert_close(out, X @ W.t(), rtol=1e-5, atol=1e-4)
+
+
+# ------------------------------------------------------------- K3 / K2
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("G", [1, 4])
+def test_full_attention_matches_torch_and_decode(dtype, G):
+    """Causal GQA attention over the paged cache vs a torch fp32 reference; the
+    T-row verify result equals T separate decode calls bit for bit."""
+    from draftkv import PagedKVCache
+    L = lib()
+    n_kv, d, n = 2, 64, 700
+    code = L.F32 if dtype == "f32" else L.BF16
+    cache = PagedKVCache(1, n_kv, d, 16, 64, dtype, batch=1)
+    rng = np.random.default_rng(G)
+    k = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    v = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    cache.append(0, k, v, np.arange(n))
+    T = 6
+    p0 = n - T
+    q = torch.from_numpy(rng.standard_normal((T, n_kv * G, d)).astype(np.float32)).cuda()
+    pos0 = torch.tensor([p0], dtype=torch.int32, device="cuda")
+    dims = cache.dims()
+    work = torch.zeros(int(L.load().dkv_attn_work_bytes(dims, G, T, cache.capacity_tokens, 128, 0)),
+                       dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, n_kv * G * d), dtype=torch.float32, device="cuda")
+    L.call("dkv_attn_full", cache.struct(), dims, 0, G, T, q.data_ptr(), pos0.data_ptr(), out.data_ptr(), L.F32,
+           128, work.data_ptr(), work.numel(), L.stream_ptr())
+    # reference
+    kk = torch.from_numpy(k).cuda().repeat_interleave(G, dim=1)
+    vv = torch.from_numpy(v).cuda().repeat_interleave(G, dim=1)
+    s = torch.einsum("qhd,khd->qhk", q, kk) / np.sqrt(d)
+    mask = torch.arange(n, device="cuda")[None, :] > (p0 + torch.arange(T, device="cuda"))[:, None]
+    s = s.masked_fill(mask[:, None, :], float("-inf"))
+    ref = torch.einsum("qhk,khd->qhd", torch.softmax(s, -1), vv).reshape(T, -1)
+    torch.testing.assert_close(out, ref, rtol=2e-5, atol=2e-5)
+    for t in range(T):
+        o1 = torch.zeros((1, n_kv * G * d), dtype=torch.float32, device="cuda")
+        pt = torch.tensor([p0 + t], dtype=torch.int32, device="cuda")
+        L.call("dkv_attn_full", cache.struct(), dims, 0, G, 1, q[t:t + 1].contiguous().data_ptr(), pt.data_ptr(),
+               o1.data_ptr(), L.F32, 128, work.data_ptr(), work.numel(), L.stream_ptr())
+        assert torch.equal(o1[0], out[t]), t

@@ -2,6 +2,8 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <vector>
+
 #include "common.cuh"
 
 namespace dkv {
@@ -34,7 +36,71 @@ uint32_t* device_error_word() {
     return cached;
 }
 
+// ------------------------------------------------------------------ profiling
+namespace {
+struct ProfRec {
+    int kind;
+    double bytes;
+    cudaEvent_t a, b;
+};
+struct Prof {
+    bool on = false;
+    int used = 0;
+    std::vector<ProfRec> recs;
+} g_prof;
+}  // namespace
+
+ProfScope::ProfScope(int kind, double bytes, cudaStream_t s) : st(s) {
+    if (!g_prof.on || g_prof.used >= (int)g_prof.recs.size()) return;
+    slot = g_prof.used++;
+    g_prof.recs[slot].kind = kind;
+    g_prof.recs[slot].bytes = bytes;
+    cudaEventRecord(g_prof.recs[slot].a, st);
+}
+
+ProfScope::~ProfScope() {
+    if (slot >= 0) cudaEventRecord(g_prof.recs[slot].b, st);
+}
+
 }  // namespace dkv
+
+extern "C" int dkv_prof_start(int max_records) {
+    using dkv::g_prof;
+    DKV_REQUIRE(max_records > 0 && max_records <= (1 << 20), "dkv_prof_start: max_records");
+    while ((int)g_prof.recs.size() < max_records) {
+        dkv::ProfRec r{};
+        DKV_CUDA(cudaEventCreate(&r.a));
+        DKV_CUDA(cudaEventCreate(&r.b));
+        g_prof.recs.push_back(r);
+    }
+    g_prof.used = 0;
+    g_prof.on = true;
+    return DKV_OK;
+}
+
+extern "C" int dkv_prof_stop(void) {
+    dkv::g_prof.on = false;
+    return DKV_OK;
+}
+
+extern "C" int dkv_prof_summary(int kind, double* total_ms, int64_t* launches, double* total_bytes) {
+    using dkv::g_prof;
+    DKV_REQUIRE(total_ms && launches && total_bytes, "dkv_prof_summary: outputs required");
+    *total_ms = 0.0;
+    *launches = 0;
+    *total_bytes = 0.0;
+    for (int i = 0; i < g_prof.used; ++i) {
+        const dkv::ProfRec& r = g_prof.recs[i];
+        if (r.kind != kind) continue;
+        DKV_CUDA(cudaEventSynchronize(r.b));
+        float ms = 0.f;
+        DKV_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        *total_ms += ms;
+        *launches += 1;
+        *total_bytes += r.bytes;
+    }
+    return DKV_OK;
+}
 
 extern "C" const char* dkv_last_error(void) { return dkv::g_err; }
 

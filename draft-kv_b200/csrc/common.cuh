@@ -56,6 +56,19 @@ inline cudaError_t allow_smem(K kernel, size_t bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
+// Raises a kernel's dynamic shared memory limit to the device's opt-in
+// maximum minus the kernel's static shared memory.
+template <typename K>
+inline cudaError_t allow_smem_max(K kernel) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Bump allocator over a caller-provided scratch buffer.
@@ -71,6 +84,16 @@ struct Arena {
         used = need;
         return reinterpret_cast<T*>(base + off);
     }
+};
+
+// ------------------------------------------------------------------ profiling
+// Optional CUDA-event timing of each launch by kernel class (dkv_prof_*).
+// When profiling is off a ProfScope costs one branch.
+struct ProfScope {
+    int slot = -1;
+    cudaStream_t st;
+    ProfScope(int kind, double bytes, cudaStream_t s);
+    ~ProfScope();
 };
 
 // ------------------------------------------------------------------ types

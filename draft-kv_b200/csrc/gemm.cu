@@ -476,6 +476,9 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     }
     cudaStream_t st = (cudaStream_t)stream;
     dim3 grid(mtiles * S, nblk);
+    // algorithmic bytes: the weights once, the activations in and out
+    const double elem = w_dtype == DKV_F32 ? 4.0 : 2.0;
+    ProfScope ps(DKV_PROF_GEMM, (double)M_real * K * elem + (double)N * K * elem + (double)N * M_real * 4.0, st);
     if (w_dtype == DKV_F32) {
         const size_t smem = std::max((size_t)kF32Tok * kF32Chunk * 4, (size_t)kF32Tok * kTileStride * 4);
         gemm_f32_kernel<<<grid, 256, smem, st>>>(g);

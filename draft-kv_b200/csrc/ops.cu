@@ -120,7 +120,8 @@ template <typename WFn>
 DKV_DEV int draw_index(WFn wfn, int V, double total, double u, double* redd, int* found) {
     const double target = u * total;
     double carry = 0.0;
-    if (threadIdx.x == 0) *found = -1;
+    constexpr int kNone = 0x7fffffff;
+    if (threadIdx.x == 0) *found = kNone;   // lowered by atomicMin on a hit
     __syncthreads();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int last_pos = -1;
@@ -152,11 +153,15 @@ DKV_DEV int draw_index(WFn wfn, int V, double total, double u, double* redd, int
         if (hit) atomicMin(found, i);
         carry += redd[nw];
         __syncthreads();
-        if (*found >= 0) break;
+        if (*found != kNone) break;
     }
     // rounding can leave the target just above the final prefix: take the
     // last index with positive weight
-    if (*found < 0) {
+    const bool none = *found == kNone;
+    __syncthreads();
+    if (none) {
+        if (threadIdx.x == 0) *found = -1;
+        __syncthreads();
         int lp = last_pos;
         for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
         if (lane == 0) atomicMax(found, lp);
@@ -167,8 +172,10 @@ DKV_DEV int draw_index(WFn wfn, int V, double total, double u, double* redd, int
     return r < 0 ? 0 : r;
 }
 
+constexpr int kRowThreads = 512;   // threads of the per-row sampling / acceptance CTAs
+
 // One CTA per row: argmax (T <= 0) or a draw from softmax(l / T).
-__global__ void sample_kernel(const float* logits, int V, float temperature, uint64_t seed, const uint64_t* counter,
+__global__ void __launch_bounds__(kRowThreads) sample_kernel(const float* logits, int V, float temperature, uint64_t seed, const uint64_t* counter,
                               int32_t* tokens, int tok_stride) {
     __shared__ ArgMax red[32];
     __shared__ double redd[33];
@@ -222,7 +229,7 @@ DKV_DEV double p_of(const RowStat& s, float l, double invT) {
     return exp(((double)l - (double)s.mx) * invT) / s.sum;
 }
 
-__global__ void accept_kernel(AcceptArgs a) {
+__global__ void __launch_bounds__(kRowThreads) accept_kernel(AcceptArgs a) {
     __shared__ ArgMax red[32];
     __shared__ double redd[33];
     __shared__ int found, is_last;
@@ -345,6 +352,7 @@ extern "C" int dkv_embed(const void* emb, int emb_dtype, const void* pos_emb, co
                          void* stream) {
     DKV_REQUIRE(emb && tokens && h && batch >= 0 && T >= 0 && dm > 0 && vocab > 0, "dkv_embed args");
     if (batch * T == 0) return DKV_OK;
+    ProfScope ps(DKV_PROF_EMBED, 0.0, (cudaStream_t)stream);
     embed_kernel<<<batch * T, 256, 0, (cudaStream_t)stream>>>(emb, emb_dtype, pos_emb, tokens, tok_stride, T, pos0,
                                                                dm, h, vocab, max_pos, device_error_word());
     DKV_LAUNCHED();
@@ -355,6 +363,7 @@ extern "C" int dkv_norm(const float* h, int N, int dm, int layernorm, const floa
                         void* x, int x_dtype, void* stream) {
     DKV_REQUIRE(h && w && x && N >= 0 && dm > 0, "dkv_norm args");
     if (N == 0) return DKV_OK;
+    ProfScope ps(DKV_PROF_NORM, (double)N * dm * (4.0 + (x_dtype == DKV_F32 ? 4.0 : 2.0)), (cudaStream_t)stream);
     norm_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
     DKV_LAUNCHED();
     return DKV_OK;
@@ -373,7 +382,9 @@ extern "C" int dkv_sample(const float* logits, int rows, int V, float temperatur
     (void)work_bytes;
     DKV_REQUIRE(logits && tokens && rows >= 0 && V > 0, "dkv_sample args");
     if (rows == 0) return DKV_OK;
-    sample_kernel<<<rows, 1024, 0, (cudaStream_t)stream>>>(logits, V, temperature, seed, counter, tokens, tok_stride);
+    ProfScope ps(DKV_PROF_SAMPLE, (double)rows * V * 4.0, (cudaStream_t)stream);
+    sample_kernel<<<rows, kRowThreads, 0, (cudaStream_t)stream>>>(logits, V, temperature, seed, counter, tokens,
+                                                                   tok_stride);
     DKV_LAUNCHED();
     return DKV_OK;
 }
@@ -384,7 +395,7 @@ extern "C" int dkv_accept(const float* verify, const float* draft_logits, int ba
                           int32_t* rs_trunc, const int32_t* active, void* work, size_t work_bytes, void* stream) {
     DKV_REQUIRE(verify && vtok && base_pos && accepted && next && batch > 0 && gamma >= 0 && V > 0, "dkv_accept args");
     DKV_REQUIRE(vstride >= gamma + 2, "dkv_accept: vstride %d < gamma+2", vstride);
-    DKV_REQUIRE(temperature <= 0.f || draft_logits, "dkv_accept: sampling needs the draft logits");
+    DKV_REQUIRE(temperature <= 0.f || gamma == 0 || draft_logits, "dkv_accept: sampling needs the draft logits");
     DKV_REQUIRE(gamma <= 63, "dkv_accept: gamma <= 63");
     Arena ar(work, work_bytes);
     AcceptArgs a;
@@ -409,7 +420,8 @@ extern "C" int dkv_accept(const float* verify, const float* draft_logits, int ba
     a.stats = ar.take<RowStat>((size_t)batch * (2 * gamma + 1));
     DKV_REQUIRE(a.stats && a.tickets, "dkv_accept: work buffer too small");
     const int rows = temperature > 0.f ? 2 * gamma + 1 : gamma + 1;
-    accept_kernel<<<dim3(rows, batch), 1024, 0, (cudaStream_t)stream>>>(a);
+    ProfScope ps(DKV_PROF_ACCEPT, (double)batch * rows * V * 4.0, (cudaStream_t)stream);
+    accept_kernel<<<dim3(rows, batch), kRowThreads, 0, (cudaStream_t)stream>>>(a);
     DKV_LAUNCHED();
     return DKV_OK;
 }

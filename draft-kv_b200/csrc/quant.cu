@@ -843,7 +843,8 @@ static int check_comp(const dkv_comp_cache* c, dkv_dims dims, int raw_elem) {
                     c->seen,
                 "drafter cache pointers must be set");
     DKV_REQUIRE(dims.d % 64 == 0 && dims.d <= 256, "head dim %d unsupported (64/128/256)", dims.d);
-    DKV_REQUIRE(c->cb_max >= dims.d * raw_elem || c->cb_max >= dims.d, "cb_max too small");
+    (void)raw_elem;   // per-layer widths are checked against cb_max in fill_cfgs
+    DKV_REQUIRE(c->cb_max >= dims.d * 2 / 8, "cb_max %d below the 2-bit width", c->cb_max);
     DKV_REQUIRE(c->cap > 0, "cap must be positive");
     return DKV_OK;
 }
@@ -876,6 +877,7 @@ extern "C" int dkv_comp_append(const dkv_comp_cache* comp, const dkv_full_cache*
     DKV_TRY(fill_cfgs(comp, nullptr, n_layer_sel, layer0, dims.d, raw_dtype == DKV_F32 ? 4 : 2, &a.cfg));
     const size_t smem = (kAppendThreads / 32) * dims.d;
     dim3 grid(n_layer_sel, dims.batch);
+    ProfScope ps(DKV_PROF_APPEND, 0.0, (cudaStream_t)stream);
     comp_append_kernel<<<grid, kAppendThreads, smem, (cudaStream_t)stream>>>(a);
     DKV_LAUNCHED();
     return DKV_OK;
@@ -902,7 +904,10 @@ extern "C" int dkv_comp_rebuild(const dkv_comp_cache* comp, const dkv_full_cache
     }
     const int warps = 8;
     dim3 grid((comp->cap + a.rows_per_cta - 1) / a.rows_per_cta, n_sel, dims.batch);
-    comp_rebuild_kernel<<<grid, warps * 32, warps * dims.d, (cudaStream_t)stream>>>(a);
+    {
+        ProfScope ps(DKV_PROF_REBUILD, 0.0, (cudaStream_t)stream);
+        comp_rebuild_kernel<<<grid, warps * 32, warps * dims.d, (cudaStream_t)stream>>>(a);
+    }
     DKV_LAUNCHED();
     // the layer-0 rebuild advances `seen` (compress.py:131-132); done after all
     // CTAs read it, in stream order

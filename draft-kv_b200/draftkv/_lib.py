@@ -64,13 +64,16 @@ class ModelS(C.Structure):
 class StepS(C.Structure):
     _fields_ = [("batch", C.c_int), ("T", C.c_int), ("tokens", vp), ("tok_stride", C.c_int),
                 ("pos0", vp), ("logits", vp), ("work", vp), ("work_bytes", C.c_size_t),
-                ("max_ctx", C.c_int)]
+                ("max_ctx", C.c_int), ("max_T", C.c_int)]
 
 
 _SIGS = {
     "dkv_last_error": (C.c_char_p, []),
     "dkv_version": (C.c_int, []),
     "dkv_device_error": (C.c_int, [C.POINTER(C.c_uint32), vp]),
+    "dkv_prof_start": (C.c_int, [C.c_int]),
+    "dkv_prof_stop": (C.c_int, []),
+    "dkv_prof_summary": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int64), C.POINTER(C.c_double)]),
     "dkv_quantize": (C.c_int, [vp, C.c_int64, C.c_int, C.c_int, vp, vp, vp, vp, vp]),
     "dkv_quantize_pack": (C.c_int, [vp, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int, vp, vp, vp]),
     "dkv_full_write": (C.c_int, [C.POINTER(FullCacheS), DimsS, C.c_int, vp, C.c_int, vp, vp, vp]),

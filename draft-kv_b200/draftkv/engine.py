@@ -85,9 +85,19 @@ class _Batch:
         self.max_ctx = max(len(p) for p in prompts) + max_new + gamma_max + 2
         m.ensure_positions(self.max_ctx)
         pages = -(-self.max_ctx // page_size)
-        self.full = eng.full_cache_factory(B, self.max_ctx) if eng.full_cache_factory else PagedKVCache(
-            m.n_layers, m.n_kv_heads, m.d_head, page_size, pages * m.n_layers * B, m.dtype, batch=B,
-            max_blocks_per_seq=pages)
+        if eng.full_cache_factory is not None:
+            # the reference's factory takes no arguments and returns one cache
+            self.full = eng.full_cache_factory()
+            if hasattr(self.full, "materialize"):
+                self.full.materialize(m.n_kv_heads, m.d_head, m.dtype)
+                self.full.grow(self.max_ctx)
+            if getattr(self.full, "batch", 1) != B:
+                raise ValueError("full_cache_factory must return a cache with one slot per sequence")
+            if self.full.capacity_tokens < self.max_ctx:
+                raise ValueError(f"full cache holds {self.full.capacity_tokens} positions < {self.max_ctx}")
+        else:
+            self.full = PagedKVCache(m.n_layers, m.n_kv_heads, m.d_head, page_size, pages * m.n_layers * B, m.dtype,
+                                     batch=B, max_blocks_per_seq=pages)
         dev = m.device
         self.vtok = torch.zeros((B, self.VS), dtype=torch.int32, device=dev)
         self.base_pos = torch.zeros((B,), dtype=torch.int32, device=dev)
@@ -105,7 +115,8 @@ class _Batch:
         self.comp: CompressedKVCache | None = None
         self.work = None
         self._cap = cap
-        self.host_read = torch.zeros((B, self.VS + 1), dtype=torch.int32, pin_memory=True)
+        self.host_acc = torch.zeros((B,), dtype=torch.int32, pin_memory=True)
+        self.host_tok = torch.zeros((B, self.VS), dtype=torch.int32, pin_memory=True)
 
     def workspace(self):
         cap = self.comp.cap if self.comp is not None else 0
@@ -228,80 +239,21 @@ class DraftKVEngine:
         return self.generate_batch([prompt], max_new_tokens, temperature, context_key)[0]
 
     def generate_batch(self, prompts: list, max_new_tokens: int, temperature: float = 0.0,
-                       context_key: str | None = None, on_round=None) -> list:
-        prompts = [list(p) for p in prompts]
-        st = self._start(prompts, max_new_tokens, temperature)
-        m = self.model
-        B = st.B
-        toks = [list(p) for p in prompts]
-        res = [GenerationResult(tokens=toks[b]) for b in range(B)]
-        comp_cfg = None
-        plen = len(prompts[0])
-        while True:
-            left = [max_new_tokens - (len(toks[b]) - plen) for b in range(B)]
-            if max(left) <= 0:
-                break
-            active = [lft > 0 for lft in left]
-            n = [len(toks[b]) for b in range(B)]
-            ctx = max(n)
-            cfg, gamma = self.controller.select(ctx, context_key)
-            gamma = min(gamma, max(min(l for l, a in zip(left, active) if a) - 1, 0), st.G)
-            st.active.copy_(torch.tensor([1 if a else 0 for a in active], dtype=torch.int32), non_blocking=True)
-            self._set_counters(st)
-            if gamma <= 0:
-                self._baseline_step(st, temperature)
-                if st.comp is not None:
-                    self._resync(st)
-                out = self._collect(st, 0)
-                for b in range(B):
-                    if not active[b]:
-                        continue
-                    toks[b].append(out[b][1][0])
-                    res[b].verify_passes += 1
-                    res[b].rounds.append(RoundLog(cfg, 0, 0, 1, n[b]))
-                continue
-            # drafter cache: create, or rebuild only the layers whose config changed
-            if st.comp is None:
-                st.comp = self._new_comp(st, cfg)
-                ctx_t = torch.tensor([n[b] - 1 for b in range(B)], dtype=torch.int32, device=m.device)
-                layers = list(range(m.n_layers))
-                self._rebuild(st, layers, ctx_t, advance=True)
-                comp_cfg = cfg
-                for r in res:
-                    r.cache_rebuilds += 1
-            elif comp_cfg != cfg:
-                old = layer_cfgs(comp_cfg, m.n_layers)
-                new = layer_cfgs(cfg, m.n_layers)
-                changed = [L for L in range(m.n_layers) if old[L] != new[L]]
-                st.comp.set_cfgs(new)
-                ctx_t = torch.tensor([n[b] - 1 for b in range(B)], dtype=torch.int32, device=m.device)
-                self._rebuild(st, changed, ctx_t, advance=0 in changed)
-                comp_cfg = cfg
-                for r in res:
-                    r.cache_rebuilds += 1
-                    r.layers_rebuilt += len(changed)
-            for b in range(B):
-                st.full.ensure(b, n[b] + gamma)
-            self._round_device(st, gamma, temperature)
-            # host bookkeeping: rollback the full cache, emitted tokens
-            out = self._collect(st, gamma)
-            for b in range(B):
-                k, emitted = out[b]
-                if not active[b]:
-                    st.full.set_length(b, n[b] - 1)
-                    continue
-                toks[b].extend(emitted)
-                st.full.set_length(b, n[b] - 1 + gamma + 1)
-                st.full.truncate_seq(b, n[b] + k)
-                self.controller.update(cfg, gamma, k, n[b], context_key)
-                res[b].draft_steps += gamma
-                res[b].verify_passes += 1
-                res[b].rounds.append(RoundLog(cfg, gamma, k, len(emitted), n[b]))
-            if on_round is not None:
-                on_round(out)
-        for b in range(B):
-            res[b].tokens = toks[b]
-        return res
+                       context_key: str | None = None, exchange=None) -> list:
+        """Decodes several same-length prompts together; one result each."""
+        sess = self.session(prompts, max_new_tokens, temperature, context_key, exchange)
+        while not sess.done:
+            sess.round()
+        return sess.results()
+
+    def session(self, prompts: list, max_new_tokens: int, temperature: float = 0.0,
+                context_key: str | None = None, exchange=None) -> "Session":
+        """Prefills `prompts` and returns a Session whose round() runs one
+        draft / verify round.  `exchange`, when given, maps this process's
+        per-sequence [(accepted, ctx)] to the list over every process (the
+        multi-GPU stats all-gather); the controller is updated with that list,
+        so replicated controllers stay identical."""
+        return Session(self, [list(p) for p in prompts], max_new_tokens, temperature, context_key, exchange)
 
     # -------------------------------------------------------- device round
     def _new_comp(self, st: _Batch, cfg) -> CompressedKVCache:
@@ -359,12 +311,111 @@ class DraftKVEngine:
 
     def _collect(self, st: _Batch, gamma: int) -> list:
         """(accepted, emitted tokens) per sequence -- the only device->host read."""
-        st.host_read[:, 0].copy_(st.accepted, non_blocking=True)
-        st.host_read[:, 1:].copy_(st.vtok, non_blocking=True)
+        st.host_acc.copy_(st.accepted, non_blocking=True)
+        st.host_tok.copy_(st.vtok, non_blocking=True)
         torch.cuda.current_stream().synchronize()
-        h = st.host_read.numpy()
+        acc = st.host_acc.numpy()
+        tok = st.host_tok.numpy()
         out = []
         for b in range(st.B):
-            k = int(h[b, 0])
-            out.append((k, [int(t) for t in h[b, 2:2 + k + 1]]))
+            k = int(acc[b])
+            # vtok[b] = [pending, drafts..., ] with the emitted stream at 1..k+1
+            out.append((k, [int(t) for t in tok[b, 1:1 + k + 1]]))
+        return out
+
+
+class Session:
+    """One batched generation in progress (see DraftKVEngine.session)."""
+
+    def __init__(self, eng: DraftKVEngine, prompts: list, max_new: int, temperature: float, key, exchange) -> None:
+        self.eng = eng
+        self.m = eng.model
+        self.T = float(temperature)
+        self.key = key
+        self.exchange = exchange
+        self.max_new = max_new
+        self.st = eng._start(prompts, max_new, temperature)
+        self.B = self.st.B
+        self.toks = [list(p) for p in prompts]
+        self.res = [GenerationResult(tokens=self.toks[b]) for b in range(self.B)]
+        self.plen = len(prompts[0])
+        self.comp_cfg = None
+        self.last = None        # (cfg, gamma, [(k, emitted)]) of the latest round
+
+    @property
+    def done(self) -> bool:
+        return all(len(t) - self.plen >= self.max_new for t in self.toks)
+
+    def results(self) -> list:
+        for b in range(self.B):
+            self.res[b].tokens = self.toks[b]
+        return self.res
+
+    def round(self) -> list:
+        """One round for every active sequence; returns [(accepted, emitted)]."""
+        eng, st, m, B = self.eng, self.st, self.m, self.B
+        left = [self.max_new - (len(self.toks[b]) - self.plen) for b in range(B)]
+        active = [lft > 0 for lft in left]
+        if not any(active):
+            return []
+        n = [len(self.toks[b]) for b in range(B)]
+        cfg, gamma = eng.controller.select(max(n), self.key)
+        gamma = min(gamma, max(min(l for l, a in zip(left, active) if a) - 1, 0), st.G)
+        st.active.copy_(torch.tensor([1 if a else 0 for a in active], dtype=torch.int32), non_blocking=True)
+        eng._set_counters(st)
+        if gamma <= 0:
+            eng._baseline_step(st, self.T)
+            if st.comp is not None:
+                eng._resync(st)
+            out = eng._collect(st, 0)
+            for b in range(B):
+                if active[b]:
+                    self.toks[b].append(out[b][1][0])
+                    self.res[b].verify_passes += 1
+                    self.res[b].rounds.append(RoundLog(cfg, 0, 0, 1, n[b]))
+            if self.exchange is not None:
+                self.exchange([])        # every process takes part in every round's exchange
+            self.last = (cfg, 0, out)
+            return out
+        # drafter cache: create, or rebuild only the layers whose config changed
+        if st.comp is None:
+            st.comp = eng._new_comp(st, cfg)
+            ctx_t = torch.tensor([n[b] - 1 for b in range(B)], dtype=torch.int32, device=m.device)
+            eng._rebuild(st, list(range(m.n_layers)), ctx_t, advance=True)
+            self.comp_cfg = cfg
+            for r in self.res:
+                r.cache_rebuilds += 1
+        elif self.comp_cfg != cfg:
+            old = layer_cfgs(self.comp_cfg, m.n_layers)
+            new = layer_cfgs(cfg, m.n_layers)
+            changed = [L for L in range(m.n_layers) if old[L] != new[L]]
+            st.comp.set_cfgs(new)
+            ctx_t = torch.tensor([n[b] - 1 for b in range(B)], dtype=torch.int32, device=m.device)
+            eng._rebuild(st, changed, ctx_t, advance=0 in changed)
+            self.comp_cfg = cfg
+            for r in self.res:
+                r.cache_rebuilds += 1
+                r.layers_rebuilt += len(changed)
+        for b in range(B):
+            st.full.ensure(b, n[b] + gamma)
+        eng._round_device(st, gamma, self.T)
+        out = eng._collect(st, gamma)            # the one device -> host read
+        stats = []
+        for b in range(B):
+            k, emitted = out[b]
+            if not active[b]:
+                st.full.set_length(b, n[b] - 1)
+                continue
+            self.toks[b].extend(emitted)
+            st.full.set_length(b, n[b] - 1 + gamma + 1)
+            st.full.truncate_seq(b, n[b] + k)        # rollback (engine.py:216)
+            stats.append((k, n[b]))
+            self.res[b].draft_steps += gamma
+            self.res[b].verify_passes += 1
+            self.res[b].rounds.append(RoundLog(cfg, gamma, k, len(emitted), n[b]))
+        if self.exchange is not None:
+            stats = self.exchange(stats)
+        for k, ctx in stats:
+            eng.controller.update(cfg, gamma, k, ctx, self.key)
+        self.last = (cfg, gamma, out)
         return out

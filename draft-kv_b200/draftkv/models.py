@@ -304,6 +304,58 @@ class GPT2(DeviceDecoder):
                             layers)
 
 
+def random_device_weights(cfg: dict, seed: int = 0, std: float = 0.02, device: str = "cuda") -> dict:
+    """N(0, std) weights generated on the device from a seeded torch generator,
+    norm gains 1, biases 0 (the benchmark's random init for shapes too large
+    for numpy).  Keys and shapes follow the reference's checkpoints; dtype is
+    the config's (bf16 / f32)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    dt = torch.bfloat16 if cfg.get("dtype", "bf16") == "bf16" else torch.float32
+
+    def R(*shape):
+        return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(dt)
+
+    def ones(n):
+        return torch.ones(n, device=device, dtype=torch.float32)
+
+    w = {}
+    if cfg["arch"] == "llama":
+        d, L, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["vocab_size"]
+        H, KV = cfg["num_attention_heads"], cfg["num_key_value_heads"]
+        D = cfg.get("head_dim") or d // H
+        F = cfg["intermediate_size"]
+        w["model.embed_tokens.weight"] = R(V, d)
+        w["model.norm.weight"] = ones(d)
+        for i in range(L):
+            p = f"model.layers.{i}."
+            w[p + "input_layernorm.weight"] = ones(d)
+            w[p + "post_attention_layernorm.weight"] = ones(d)
+            w[p + "self_attn.q_proj.weight"] = R(H * D, d)
+            w[p + "self_attn.k_proj.weight"] = R(KV * D, d)
+            w[p + "self_attn.v_proj.weight"] = R(KV * D, d)
+            w[p + "self_attn.o_proj.weight"] = R(d, H * D)
+            w[p + "mlp.gate_proj.weight"] = R(F, d)
+            w[p + "mlp.up_proj.weight"] = R(F, d)
+            w[p + "mlp.down_proj.weight"] = R(d, F)
+        if not cfg.get("tie_word_embeddings", True):
+            w["lm_head.weight"] = R(V, d)
+    else:
+        d, L, V, F = cfg["n_embd"], cfg["n_layer"], cfg["vocab_size"], cfg["n_inner"]
+        zeros = lambda n: torch.zeros(n, device=device, dtype=torch.float32)  # noqa: E731
+        w["wte.weight"] = R(V, d)
+        w["wpe.weight"] = R(cfg["n_positions"], d)
+        for i in range(L):
+            p = f"h.{i}."
+            w[p + "ln_1.weight"], w[p + "ln_1.bias"] = ones(d), zeros(d)
+            w[p + "attn.c_attn.weight"], w[p + "attn.c_attn.bias"] = R(d, 3 * d), zeros(3 * d)
+            w[p + "attn.c_proj.weight"], w[p + "attn.c_proj.bias"] = R(d, d), zeros(d)
+            w[p + "ln_2.weight"], w[p + "ln_2.bias"] = ones(d), zeros(d)
+            w[p + "mlp.c_fc.weight"], w[p + "mlp.c_fc.bias"] = R(d, F), zeros(F)
+            w[p + "mlp.c_proj.weight"], w[p + "mlp.c_proj.bias"] = R(F, d), zeros(d)
+        w["ln_f.weight"], w["ln_f.bias"] = ones(d), zeros(d)
+    return w
+
+
 def from_config(weights: dict, config: dict, **kw) -> DeviceDecoder:
     """GPT2 or LlamaLike by the config's keys."""
     return (GPT2 if "n_embd" in config else LlamaLike)(weights, config, **kw)

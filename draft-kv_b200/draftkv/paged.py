@@ -83,6 +83,8 @@ def dtype_code(dtype) -> int:
     """DKV_F32 / DKV_BF16 from a numpy / torch dtype or a name."""
     if dtype is None:
         return _lib.F32
+    if isinstance(dtype, int) and dtype in (_lib.F32, _lib.BF16):
+        return dtype
     if isinstance(dtype, str):
         return {"f32": _lib.F32, "float32": _lib.F32, "bf16": _lib.BF16, "bfloat16": _lib.BF16}[dtype]
     if torch is not None and dtype == torch.bfloat16:

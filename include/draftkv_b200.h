@@ -61,8 +61,22 @@ enum { DKV_ARCH_LLAMA = 0, DKV_ARCH_GPT2 = 1 };
 /* ------------------------------------------------------------ plumbing */
 DKV_API const char* dkv_last_error(void);
 DKV_API int dkv_version(void);
-/* Reads and clears the device error word that bounded waits write. */
+/* Reads and clears the device error word kernels set instead of trapping:
+ * 0x10 append rows over the per-call limit, 0x20 drafter slot capacity,
+ * 0x100 token id outside the vocabulary, 0x200 position outside the table. */
 DKV_API int dkv_device_error(uint32_t* out_code, void* stream);
+
+/* Launch timing by kernel class with CUDA events on the launching stream
+ * (no library counterpart in the reference, which has no profiler: it serves
+ * the roofline numbers).  start() creates up to max_records event pairs and
+ * enables recording; summary() waits for the events and sums one class. */
+enum {
+    DKV_PROF_GEMM = 0, DKV_PROF_ATTN_FULL = 1, DKV_PROF_ATTN_COMP = 2, DKV_PROF_APPEND = 3,
+    DKV_PROF_REBUILD = 4, DKV_PROF_NORM = 5, DKV_PROF_EMBED = 6, DKV_PROF_SAMPLE = 7, DKV_PROF_ACCEPT = 8
+};
+DKV_API int dkv_prof_start(int max_records);
+DKV_API int dkv_prof_stop(void);
+DKV_API int dkv_prof_summary(int kind, double* total_ms, int64_t* launches, double* total_bytes);
 
 /* ------------------------------------------------------------ K1 quantize
  * Replaces draftkv/compress.py:21-46 `quantize(x, bits, group=64)`.

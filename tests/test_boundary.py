@@ -58,6 +58,31 @@ def test_argument_errors_are_reported_not_faulted(lib):
     assert st == _lib.EINVAL and b"bits" in lib.dkv_last_error()
 
 
+def header_struct_fields():
+    """Field names of each `typedef struct {...} name;` in the header."""
+    txt = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for body, name in re.findall(r"typedef struct\s*\{(.*?)\}\s*(\w+);", txt, flags=re.S):
+        fields = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            for part in decl.split(","):
+                m = re.search(r"(\w+)\s*$", part.strip())
+                if m:
+                    fields.append(m.group(1))
+        out[name] = fields
+    return out
+
+
+def test_ctypes_mirrors_every_header_field():
+    hdr = header_struct_fields()
+    assert set(hdr) == set(STRUCTS)
+    for cname, cls in STRUCTS.items():
+        assert [f for f, _ in cls._fields_] == hdr[cname], cname
+
+
 def test_struct_layouts_match_the_header(tmp_path):
     prog = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for cname, cls in STRUCTS.items():

@@ -12,44 +12,9 @@
 // it serves fp32 models and shapes the tensor-core kernels do not cover.
 #include "common.cuh"
 
+#include "attn_common.cuh"
+
 namespace dkv {
-
-struct KeySrc {
-    // full cache
-    const void* k_pool;
-    const void* v_pool;
-    const int32_t* page_table;
-    int page_size, max_pages, dtype;
-    // drafter cache
-    const uint8_t* k_codes;
-    const uint8_t* v_codes;
-    const uint16_t* k_sl;
-    const uint16_t* v_sl;
-    const int32_t* cpos;
-    const int32_t* meta;
-    int cap, cb_max, bits;
-    bool comp;
-};
-
-struct AttnArgs {
-    KeySrc src;
-    int n_layers, n_kv, d, layer, group, T, batch;
-    const float* q;          // [batch*T][n_kv*group][d]
-    const int32_t* qpos0;    // [batch]
-    void* out;
-    int out_dtype;
-    int split;               // keys (full) or slots (drafter) per split
-    int n_splits;
-    int n_rb;                // query row blocks per (sequence, head)
-    float scale;
-    // scratch
-    float* part;             // [batch][n_kv][n_splits][R][d + 2]
-    unsigned* tickets;       // [batch][n_kv]  (+ [batch] head tickets for the fold)
-    float* sbuf;             // drafter: raw scores [batch][n_kv][group][cap]
-    float* mass;             // drafter: [batch][n_layers][n_kv][cap]
-    float* score;            // drafter: [batch][n_layers][cap]
-    unsigned* fold_tickets;  // [batch]
-};
 
 DKV_DEV float deq_code(const uint8_t* codes, const uint16_t* sl, int d, int bits, bool k_order, int e, int raw) {
     int p = e;
@@ -82,7 +47,7 @@ DKV_DEV float deq_code(const uint8_t* codes, const uint16_t* sl, int d, int bits
 
 constexpr int kGenKT = 32;     // keys per tile
 constexpr int kGenThreads = 128;
-constexpr int kGenRB = 64;     // query rows per CTA
+constexpr int kGenRB = kAttnRB;   // query rows per CTA
 
 // smem: Q[R][d] | K[KT][d+1] | V[KT][d+1] | P[R][KT] | m[R] l[R] a[R] | O[R][d] | kp[KT]
 // Rows (query token x group head) are processed in blocks of at most kGenRB
@@ -210,49 +175,10 @@ __global__ void __launch_bounds__(kGenThreads) attn_generic_kernel(AttnArgs a) {
         mypart[r * PS + 0] = ms[r];
         mypart[r * PS + 1] = ls[r];
     }
-    __threadfence();
-    __syncthreads();
-    __shared__ int is_last;
-    if (threadIdx.x == 0) {
-        unsigned* tk = a.tickets + bhr;
-        const unsigned prev = atomicAdd(tk, 1u);
-        is_last = prev == (unsigned)(a.n_splits - 1);
-        if (is_last) *tk = 0u;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    const float* parts = a.part + (bhr * a.n_splits) * kGenRB * PS;
-    // per row: global max and sum over splits (split order)
-    for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        float M = -INFINITY;
-        for (int q = 0; q < a.n_splits; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * kGenRB + r) * PS));
-        float L = 0.f;
-        for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * kGenRB + r) * PS);
-            if (mq == -INFINITY) continue;
-            L += __ldcg(parts + ((size_t)q * kGenRB + r) * PS + 1) * expf(mq - M);
-        }
-        ms[r] = M;
-        ls[r] = L;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < R * d; i += blockDim.x) {
-        const int r = i / d, e = i % d;
-        const float M = ms[r];
-        float acc = 0.f;
-        for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * kGenRB + r) * PS);
-            if (mq == -INFINITY) continue;
-            acc += __ldcg(parts + ((size_t)q * kGenRB + r) * PS + 2 + e) * expf(mq - M);
-        }
-        const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
-        const int t = (r0 + r) / G, g = (r0 + r) % G;
-        store_from_f32(a.out, a.out_dtype, (((size_t)b * T + t) * HQ + h * G + g) * d + e, o);
-    }
+    if (!split_merge(a, bhr, b, h, R, r0, ms, ls)) return;
     if (!a.sbuf) return;
     // ---- drafter: attention mass per slot for this head (sum over the group)
-    __syncthreads();
+    __shared__ int is_last;
     float* mass_h = a.mass + (bl * a.n_kv + h) * (size_t)src.cap;
     for (int slot = threadIdx.x; slot < n_keys; slot += blockDim.x) {
         float mval = 0.f;
@@ -379,7 +305,8 @@ static int launch_generic(AttnArgs& a, dkv_dims dims, void* work, size_t work_by
 namespace dkv {
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
                  bool* handled);
-int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled);
+int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled,
+                 uint32_t* comp_tickets, int raw_dtype);
 }
 
 extern "C" int dkv_attn_full(const dkv_full_cache* full, dkv_dims dims, int layer, int group, int T, const float* q,
@@ -433,7 +360,9 @@ extern "C" int dkv_attn_comp(const dkv_comp_cache* comp, dkv_dims dims, int laye
     a.mass = comp->mass;
     a.score = comp->score;
     bool handled = false;
-    DKV_TRY(attn_comp_tc(a, dims, work, work_bytes, (cudaStream_t)stream, &handled));
+    // 16-bit entries are stored in the model dtype: 4-byte elements mean fp32
+    const int raw_dtype = comp->cb_max >= dims.d * 4 ? DKV_F32 : DKV_BF16;
+    DKV_TRY(attn_comp_tc(a, dims, work, work_bytes, (cudaStream_t)stream, &handled, comp->tickets, raw_dtype));
     if (handled) return DKV_OK;
     return launch_generic(a, dims, work, work_bytes, comp->cap, true, (cudaStream_t)stream);
 }

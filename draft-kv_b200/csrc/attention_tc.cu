@@ -1,31 +1,315 @@
-// Tensor-core attention kernels (bf16 caches): verify / baseline over the
-// paged full cache, and the drafter over quantized slots.  Shapes they do not
-// cover report handled = false and the generic kernel runs instead.
-#include "common.cuh"
+// Tensor-core attention over the paged full cache (bf16): verify, baseline
+// decode and prefill chunks.  Replaces draftkv/llama.py:202-219 /
+// draftkv/gpt2.py:197-207 over FullKVCache / PagedKVCache.
+//
+// One CTA per (key split, KV head, sequence x row block); 4 warps.  K/V pages
+// of the split stream through a double-buffered, XOR-swizzled shared-memory
+// tile of 64 keys with cp.async; warp w owns query rows [16w, 16w+16) of the
+// CTA (rows = token x GQA head) and runs S = Q K^T and O += P V with
+// mma.sync.m16n8k16 (bf16 in, fp32 accumulate) and a per-row online softmax.
+// The CTA partials merge in split order (split_merge), so a row's result does
+// not depend on how many rows share the launch: verify row i equals the
+// one-token decode at that position bit for bit.
+#include "attn_common.cuh"
 
 namespace dkv {
-struct AttnArgs;
-struct dkv_dims_fwd;
+
+DKV_DEV uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+DKV_DEV void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+DKV_DEV void ldsm4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(s));
+}
+DKV_DEV void ldsm4t(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(s));
+}
+DKV_DEV void cpasync16(void* smem, const void* gmem, bool pred) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(pred ? 16 : 0));
+}
+
+constexpr int kTcKT = 64;          // keys per tile
+constexpr int kTcThreads = 128;    // 4 warps x 16 query rows
+
+// swizzled element offset of (key, 16-byte chunk) in a [keys][D] bf16 tile
+template <int D>
+DKV_DEV int swz(int key, int chunk) {
+    return key * D + ((chunk ^ (key & 7)) << 3);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTcThreads) attn_full_tc_kernel(AttnArgs a) {
+    constexpr int DC = D / 8;      // 16-byte chunks per key row
+    constexpr int KS = D / 16;     // k16 steps over d
+    extern __shared__ __align__(128) uint8_t tsm[];
+    __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(tsm);        // [2][KT][D]
+    __nv_bfloat16* Vs = Ks + 2 * kTcKT * D;                             // [2][KT][D]
+    float* ms = reinterpret_cast<float*>(Vs + 2 * kTcKT * D);          // [kAttnRB]
+    float* ls = ms + kAttnRB;
+
+    const int s = blockIdx.x, h = blockIdx.y;
+    const int b = blockIdx.z / a.n_rb, rb = blockIdx.z % a.n_rb;
+    const int G = a.group, T = a.T;
+    const int r0 = rb * kAttnRB;
+    const int R = min(kAttnRB, T * G - r0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qr = lane >> 2, qc = lane & 3;
+    const int qbase = a.qpos0[b];
+    const int n_keys = qbase + T;
+    const int k0 = s * a.split;
+    const int k1 = min(n_keys, k0 + a.split);
+    const size_t bl = (size_t)b * a.n_layers + a.layer;
+    const int HQ = a.n_kv * G;
+    const KeySrc& src = a.src;
+    const __nv_bfloat16* kpool = reinterpret_cast<const __nv_bfloat16*>(src.k_pool);
+    const __nv_bfloat16* vpool = reinterpret_cast<const __nv_bfloat16*>(src.v_pool);
+    const bool active = warp * 16 < R;
+
+    // ---- Q fragments of this warp's 16 rows (bf16, rows >= R are zero)
+    uint32_t qf[KS][4];
+    {
+        const int rA = warp * 16 + qr, rB = rA + 8;
+        const float* qa = nullptr;
+        const float* qb = nullptr;
+        if (rA < R) {
+            const int t = (r0 + rA) / G, g = (r0 + rA) % G;
+            qa = a.q + (((size_t)b * T + t) * HQ + h * G + g) * D;
+        }
+        if (rB < R) {
+            const int t = (r0 + rB) / G, g = (r0 + rB) % G;
+            qb = a.q + (((size_t)b * T + t) * HQ + h * G + g) * D;
+        }
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int d0 = kk * 16 + 2 * qc;
+            qf[kk][0] = qa ? pack_bf16(qa[d0], qa[d0 + 1]) : 0u;
+            qf[kk][1] = qb ? pack_bf16(qb[d0], qb[d0 + 1]) : 0u;
+            qf[kk][2] = qa ? pack_bf16(qa[d0 + 8], qa[d0 + 9]) : 0u;
+            qf[kk][3] = qb ? pack_bf16(qb[d0 + 8], qb[d0 + 9]) : 0u;
+        }
+    }
+    // query positions of the two rows this thread accumulates
+    const int rowA = warp * 16 + qr, rowB = rowA + 8;
+    const int qpA = qbase + (r0 + rowA) / G, qpB = qbase + (r0 + rowB) / G;
+
+    float o[D / 8][4];
+#pragma unroll
+    for (int j = 0; j < D / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+
+    const int ntiles = k1 > k0 ? (k1 - k0 + kTcKT - 1) / kTcKT : 0;
+    auto load_tile = [&](int buf, int t0) {
+        __nv_bfloat16* kd = Ks + buf * kTcKT * D;
+        __nv_bfloat16* vd = Vs + buf * kTcKT * D;
+        for (int i = threadIdx.x; i < kTcKT * DC; i += kTcThreads) {
+            const int key = i / DC, ch = i % DC;
+            const int kp = t0 + key;
+            const bool ok = kp < k1;
+            size_t off = 0;
+            if (ok) {
+                const int page = src.page_table[bl * src.max_pages + kp / src.page_size];
+                off = (((size_t)page * a.n_kv + h) * src.page_size + kp % src.page_size) * D + ch * 8;
+            }
+            cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
+            cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
+        }
+        asm volatile("cp.async.commit_group;\n" ::);
+    };
+
+    if (ntiles > 0) load_tile(0, k0);
+    for (int it = 0; it < ntiles; ++it) {
+        const int t0 = k0 + it * kTcKT;
+        if (it + 1 < ntiles) {
+            load_tile((it + 1) & 1, t0 + kTcKT);
+            asm volatile("cp.async.wait_group 1;\n" ::);
+        } else {
+            asm volatile("cp.async.wait_group 0;\n" ::);
+        }
+        __syncthreads();
+        if (active) {
+            const __nv_bfloat16* kt = Ks + (it & 1) * kTcKT * D;
+            const __nv_bfloat16* vt = Vs + (it & 1) * kTcKT * D;
+            // ---- S = Q K^T over 64 keys (8 n8 tiles)
+            float sc[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+            const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+            for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    uint32_t b0, b1, b2, b3;
+                    const int key = np * 16 + (mi >> 1) * 8 + ri;
+                    ldsm4(b0, b1, b2, b3, kt + swz<D>(key, 2 * kk + (mi & 1)));
+                    mma_bf16_16816(sc[2 * np], qf[kk], b0, b1);
+                    mma_bf16_16816(sc[2 * np + 1], qf[kk], b2, b3);
+                }
+            }
+            // ---- scale, causal / range mask, online softmax (rows A and B)
+            float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int key = t0 + 8 * j + 2 * qc + (e & 1);
+                    const int qp = e < 2 ? qpA : qpB;
+                    float v = sc[j][e] * a.scale;
+                    if (key >= k1 || key > qp) v = -INFINITY;
+                    sc[j][e] = v;
+                }
+                mxA = fmaxf(mxA, fmaxf(sc[j][0], sc[j][1]));
+                mxB = fmaxf(mxB, fmaxf(sc[j][2], sc[j][3]));
+            }
+            mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 1));
+            mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, 2));
+            mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 1));
+            mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, 2));
+            const float nmA = fmaxf(mA, mxA), nmB = fmaxf(mB, mxB);
+            const float alA = nmA == -INFINITY ? 1.f : expf(mA - nmA);
+            const float alB = nmB == -INFINITY ? 1.f : expf(mB - nmB);
+            float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float nm = e < 2 ? nmA : nmB;
+                    const float p = sc[j][e] == -INFINITY ? 0.f : expf(sc[j][e] - nm);
+                    sc[j][e] = p;
+                }
+                sumA += sc[j][0] + sc[j][1];
+                sumB += sc[j][2] + sc[j][3];
+            }
+            sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+            sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+            sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+            sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+            lA = lA * alA + sumA;
+            lB = lB * alB + sumB;
+            mA = nmA;
+            mB = nmB;
+#pragma unroll
+            for (int j = 0; j < D / 8; ++j) {
+                o[j][0] *= alA;
+                o[j][1] *= alA;
+                o[j][2] *= alB;
+                o[j][3] *= alB;
+            }
+            // ---- O += P V (4 k16 steps over the 64 keys)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                uint32_t pa[4];
+                pa[0] = pack_bf16(sc[2 * ks][0], sc[2 * ks][1]);
+                pa[1] = pack_bf16(sc[2 * ks][2], sc[2 * ks][3]);
+                pa[2] = pack_bf16(sc[2 * ks + 1][0], sc[2 * ks + 1][1]);
+                pa[3] = pack_bf16(sc[2 * ks + 1][2], sc[2 * ks + 1][3]);
+#pragma unroll
+                for (int dp = 0; dp < D / 16; ++dp) {
+                    uint32_t b0, b1, b2, b3;
+                    const int key = ks * 16 + (mi & 1) * 8 + ri;
+                    ldsm4t(b0, b1, b2, b3, vt + swz<D>(key, 2 * dp + (mi >> 1)));
+                    mma_bf16_16816(o[2 * dp], pa, b0, b1);
+                    mma_bf16_16816(o[2 * dp + 1], pa, b2, b3);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- partials (rows < R), then the split merge
+    const int PS = D + 2;
+    const size_t bhr = ((size_t)b * a.n_kv + h) * a.n_rb + rb;
+    float* mypart = a.part + ((bhr * a.n_splits + s) * kAttnRB) * PS;
+    if (active) {
+        if (rowA < R) {
+#pragma unroll
+            for (int j = 0; j < D / 8; ++j) {
+                mypart[rowA * PS + 2 + 8 * j + 2 * qc] = o[j][0];
+                mypart[rowA * PS + 2 + 8 * j + 2 * qc + 1] = o[j][1];
+            }
+            if (qc == 0) {
+                mypart[rowA * PS] = mA;
+                mypart[rowA * PS + 1] = lA;
+            }
+        }
+        if (rowB < R) {
+#pragma unroll
+            for (int j = 0; j < D / 8; ++j) {
+                mypart[rowB * PS + 2 + 8 * j + 2 * qc] = o[j][2];
+                mypart[rowB * PS + 2 + 8 * j + 2 * qc + 1] = o[j][3];
+            }
+            if (qc == 0) {
+                mypart[rowB * PS] = mB;
+                mypart[rowB * PS + 1] = lB;
+            }
+        }
+    }
+    split_merge(a, bhr, b, h, R, r0, ms, ls);
+}
+
+template <int D>
+size_t full_tc_smem() {
+    return (size_t)4 * kTcKT * D * 2 + 2 * kAttnRB * sizeof(float);
+}
+
+int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
+                 bool* handled);
+int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled);
+
+constexpr size_t kAttnTicketsTc = 16384;   // same fixed ticket region as the generic kernel
 
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
                  bool* handled) {
-    (void)a;
-    (void)dims;
-    (void)work;
-    (void)work_bytes;
-    (void)max_keys;
-    (void)st;
     *handled = false;
+    if (a.src.dtype != DKV_BF16 || (dims.d != 64 && dims.d != 128) || a.split % kTcKT != 0) return DKV_OK;
+    const int R = a.T * a.group;
+    a.n_rb = (R + kAttnRB - 1) / kAttnRB;
+    a.n_splits = (max_keys + a.split - 1) / a.split;
+    if (a.n_splits < 1) a.n_splits = 1;
+    const size_t n_tk = (size_t)dims.batch * dims.n_kv * a.n_rb;
+    DKV_REQUIRE(n_tk + dims.batch <= kAttnTicketsTc, "attention: batch x heads x row blocks too large");
+    Arena ar(work, work_bytes);
+    unsigned* tk = ar.take<unsigned>(kAttnTicketsTc);
+    a.tickets = tk;
+    a.fold_tickets = tk ? tk + n_tk : nullptr;
+    a.part = ar.take<float>(n_tk * a.n_splits * kAttnRB * (dims.d + 2));
+    a.sbuf = nullptr;
+    DKV_REQUIRE(a.part && a.tickets, "attention: work buffer too small (%zu bytes)", work_bytes);
+    dim3 grid(a.n_splits, dims.n_kv, dims.batch * a.n_rb);
+    ProfScope ps(DKV_PROF_ATTN_FULL, 0.0, st);
+    if (dims.d == 128) {
+        static bool attr = false;
+        if (!attr) {
+            DKV_CUDA(allow_smem_max(attn_full_tc_kernel<128>));
+            attr = true;
+        }
+        attn_full_tc_kernel<128><<<grid, kTcThreads, full_tc_smem<128>(), st>>>(a);
+    } else {
+        static bool attr = false;
+        if (!attr) {
+            DKV_CUDA(allow_smem_max(attn_full_tc_kernel<64>));
+            attr = true;
+        }
+        attn_full_tc_kernel<64><<<grid, kTcThreads, full_tc_smem<64>(), st>>>(a);
+    }
+    DKV_LAUNCHED();
+    *handled = true;
     return DKV_OK;
 }
 
-int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled) {
-    (void)a;
-    (void)dims;
-    (void)work;
-    (void)work_bytes;
-    (void)st;
-    *handled = false;
-    return DKV_OK;
-}
 }  // namespace dkv

@@ -1,0 +1,98 @@
+// Arguments and the split merge shared by the attention kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace dkv {
+
+struct KeySrc {
+    // full cache
+    const void* k_pool;
+    const void* v_pool;
+    const int32_t* page_table;
+    int page_size, max_pages, dtype;
+    // drafter cache
+    const uint8_t* k_codes;
+    const uint8_t* v_codes;
+    const uint16_t* k_sl;
+    const uint16_t* v_sl;
+    const int32_t* cpos;
+    const int32_t* meta;
+    int cap, cb_max, bits;
+    bool comp;
+};
+
+struct AttnArgs {
+    KeySrc src;
+    int n_layers, n_kv, d, layer, group, T, batch;
+    const float* q;          // [batch*T][n_kv*group][d]
+    const int32_t* qpos0;    // [batch]
+    void* out;
+    int out_dtype;
+    int split;               // keys (full) or slots (drafter) per split
+    int n_splits;
+    int n_rb;                // query row blocks per (sequence, head)
+    float scale;
+    // scratch
+    float* part;             // [batch][n_kv][n_rb][n_splits][kAttnRB][d + 2]
+    unsigned* tickets;       // [batch][n_kv][n_rb]  (+ [batch] head tickets for the fold)
+    float* sbuf;             // drafter: raw scores [batch][n_kv][group][cap]
+    float* mass;             // drafter: [batch][n_layers][n_kv][cap]
+    float* score;            // drafter: [batch][n_layers][cap]
+    unsigned* fold_tickets;  // [batch]
+};
+
+constexpr int kAttnRB = 64;   // query rows (token x group head) per CTA
+
+// After a CTA has stored its partial rows (m, l, unnormalised O) for split s
+// of (sequence, head, row block) `bhr`, the last CTA to arrive merges every
+// split in split order (splits with no live key skipped), writes the output
+// rows and returns true with the merged max / sum in ms / ls (R rows).
+// The merge order is fixed, so a row's result is the same whatever the number
+// of rows or splits that share the launch.
+DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int r0, float* ms, float* ls) {
+    const int d = a.d, G = a.group, T = a.T, PS = d + 2, HQ = a.n_kv * G;
+    __threadfence();
+    __syncthreads();
+    __shared__ int is_last;
+    if (threadIdx.x == 0) {
+        unsigned* tk = a.tickets + bhr;
+        const unsigned prev = atomicAdd(tk, 1u);
+        is_last = prev == (unsigned)(a.n_splits - 1);
+        if (is_last) *tk = 0u;
+    }
+    __syncthreads();
+    if (!is_last) return false;
+    __threadfence();
+    const float* parts = a.part + (bhr * a.n_splits) * kAttnRB * PS;
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+        float M = -INFINITY;
+        for (int q = 0; q < a.n_splits; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * kAttnRB + r) * PS));
+        float L = 0.f;
+        for (int q = 0; q < a.n_splits; ++q) {
+            const float mq = __ldcg(parts + ((size_t)q * kAttnRB + r) * PS);
+            if (mq == -INFINITY) continue;
+            L += __ldcg(parts + ((size_t)q * kAttnRB + r) * PS + 1) * expf(mq - M);
+        }
+        ms[r] = M;
+        ls[r] = L;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * d; i += blockDim.x) {
+        const int r = i / d, e = i % d;
+        const float M = ms[r];
+        float acc = 0.f;
+        for (int q = 0; q < a.n_splits; ++q) {
+            const float mq = __ldcg(parts + ((size_t)q * kAttnRB + r) * PS);
+            if (mq == -INFINITY) continue;
+            acc += __ldcg(parts + ((size_t)q * kAttnRB + r) * PS + 2 + e) * expf(mq - M);
+        }
+        const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
+        const int t = (r0 + r) / G, g = (r0 + r) % G;
+        store_from_f32(a.out, a.out_dtype, (((size_t)b * T + t) * HQ + h * G + g) * d + e, o);
+    }
+    __syncthreads();
+    return true;
+}
+
+}  // namespace dkv

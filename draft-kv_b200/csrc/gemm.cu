@@ -25,7 +25,8 @@
 namespace dkv {
 
 constexpr int kTileM = 128;     // weight rows per CTA (8 warps x 16)
-constexpr int kChunkK = 128;    // k elements per staged X chunk
+constexpr int kChunkK = 256;    // k elements per staged X chunk
+constexpr int kChunkSteps = kChunkK / 16;   // k16 steps per chunk = weight prefetch depth
 constexpr int kTileStride = 132;  // smem row stride (floats) of the result tile [n][m]
 // Split-K tickets occupy a fixed region at the start of every GEMM work
 // buffer, so consecutive calls of any shape see them zero (each launch
@@ -160,6 +161,7 @@ struct GemmArgs {
     int M, N, K, S;
     float* ws;
     unsigned* tickets;
+    uint32_t* err;      // device error word (bounded waits)
     EpiArgs epi;
 };
 
@@ -194,11 +196,61 @@ DKV_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)
 // X chunk row stride in bf16 elements (128 + 8 padding: conflict-free ldmatrix)
 constexpr int kXStride = kChunkK + 8;
 
+// ---- mbarrier / bulk-copy helpers (TMA without multicast)
+DKV_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+DKV_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+DKV_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+DKV_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+DKV_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+DKV_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after ~2^22 polls (each poll may suspend briefly),
+// records 0x80 in the device error word and returns false.
+DKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicOr(err, 0x80u);
+    return false;
+}
+
+constexpr int kWChunkBytes = kChunkSteps * 512;   // one warp's weights for one X chunk
+
+// Weight stages per warp: deeper for few tokens (small X chunks).
+template <int NT>
+__host__ __device__ constexpr int gemm_stages() {
+    return NT <= 2 ? 3 : 2;
+}
+template <int NT>
+__host__ __device__ constexpr size_t gemm_smem() {
+    return (size_t)2 * 8 * NT * kXStride * 2 + (size_t)8 * gemm_stages<NT>() * kWChunkBytes + 8 * 8 * sizeof(uint64_t);
+}
+
 template <int NT>   // number of n8 token tiles per CTA (tokens = 8*NT)
 __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
-    extern __shared__ __align__(16) uint8_t gsm[];
+    extern __shared__ __align__(128) uint8_t gsm[];
     constexpr int NB = 8 * NT;
+    constexpr int NST = gemm_stages<NT>();
     uint16_t* xs = reinterpret_cast<uint16_t*>(gsm);          // [2][NB][kXStride]
+    uint8_t* wst = gsm + (size_t)2 * NB * kXStride * 2;       // [8 warps][NST][kWChunkBytes]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wst + (size_t)8 * NST * kWChunkBytes);   // [8][NST]
     const int mtiles = g.M / kTileM;
     const int mtile = blockIdx.x % mtiles, s = blockIdx.x / mtiles;
     const int nblk = blockIdx.y, n0 = nblk * 64;
@@ -206,6 +258,25 @@ __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
     const int kt0 = (int)((long long)s * KT / g.S), kt1 = (int)((long long)(s + 1) * KT / g.S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint16_t* X = reinterpret_cast<const uint16_t*>(g.x);
+    const int nsteps = kt1 - kt0;
+    const int nchunks = (nsteps + kChunkSteps - 1) / kChunkSteps;
+    // this warp's weight stream: 16 rows x [kt0, kt1) is one contiguous byte range
+    const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(g.w) + ((size_t)(mtile * 8 + warp) * KT + kt0) * 512;
+    uint8_t* my_st = wst + (size_t)warp * NST * kWChunkBytes;
+    uint64_t* my_bar = bars + warp * NST;
+    auto issue = [&](int ch) {    // lane 0 only
+        const int steps = min(kChunkSteps, nsteps - ch * kChunkSteps);
+        const uint32_t bytes = (uint32_t)steps * 512u;
+        uint64_t* bar = my_bar + (ch % NST);
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(my_st + (size_t)(ch % NST) * kWChunkBytes, wsrc + (size_t)ch * kWChunkBytes, bytes, bar);
+    };
+    if (lane == 0) {
+        for (int i = 0; i < NST; ++i) mbar_init(my_bar + i, 1);
+        fence_async_shared();
+        for (int ch = 0; ch < NST && ch < nchunks; ++ch) issue(ch);
+    }
+    __syncwarp();
 
     // X chunk loader: rows n0..n0+NB-1, k range [k_lo, k_lo + 128)
     auto load_chunk = [&](int buf, int k_lo) {
@@ -223,30 +294,25 @@ __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
-    const uint4* W = reinterpret_cast<const uint4*>(g.w) + ((size_t)(mtile * 8 + warp) * KT) * 32 + lane;
-    constexpr int PF = 8;
-    uint4 ring[PF];
-#pragma unroll
-    for (int i = 0; i < PF; ++i)
-        if (kt0 + i < kt1) ring[i] = __ldcs(W + (size_t)(kt0 + i) * 32);
-
-    const int nchunks = (kt1 - kt0 + 7) / 8;
+    bool ok_all = true;
     if (nchunks > 0) load_chunk(0, kt0 * 16);
     for (int ch = 0; ch < nchunks; ++ch) {
         if (ch + 1 < nchunks) {
-            load_chunk((ch + 1) & 1, (kt0 + (ch + 1) * 8) * 16);
+            load_chunk((ch + 1) & 1, (kt0 + (ch + 1) * kChunkSteps) * 16);
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
         }
         __syncthreads();
         const uint16_t* xb = xs + (ch & 1) * NB * kXStride;
+        const bool ready = mbar_wait(my_bar + (ch % NST), (uint32_t)((ch / NST) & 1), g.err);
+        ok_all = ok_all && ready;
+        const uint4* wa = reinterpret_cast<const uint4*>(my_st + (size_t)(ch % NST) * kWChunkBytes) + lane;
 #pragma unroll
-        for (int i = 0; i < PF; ++i) {
-            const int kt = kt0 + ch * 8 + i;
-            if (kt < kt1) {
-                const uint4 a = ring[i];
-                if (kt + PF < kt1) ring[i] = __ldcs(W + (size_t)(kt + PF) * 32);
+        for (int i = 0; i < kChunkSteps; ++i) {
+            const int kt = kt0 + ch * kChunkSteps + i;
+            if (kt < kt1 && ready) {
+                const uint4 a = wa[i * 32];
                 const int kc = i * 16;   // k offset within chunk
 #pragma unroll
                 for (int j = 0; j + 1 < NT; j += 2) {
@@ -266,8 +332,21 @@ __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
                 }
             }
         }
+        // this stage is consumed: refill it with chunk ch + NST
+        __syncwarp();
+        if (lane == 0 && ch + NST < nchunks && ok_all) {
+            fence_async_shared();
+            issue(ch + NST);
+        }
         __syncthreads();
     }
+    if (!ok_all && lane == 0) {
+        // a copy never completed: wait (bounded) for any still in flight
+        // before the shared memory is reused or released
+        for (int ch = max(0, nchunks - NST); ch < nchunks; ++ch)
+            mbar_wait(my_bar + (ch % NST), (uint32_t)((ch / NST) & 1), nullptr);
+    }
+    __syncthreads();
 
     // result tile T[n][m] in shared memory (reuses the X buffers)
     float* tile = reinterpret_cast<float*>(gsm);
@@ -366,14 +445,33 @@ __global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int M, int K,
     }
 }
 
+// K split S for an (M, K) GEMM.  One CTA per SM is resident (the weight
+// stages fill shared memory), so S is chosen for wave quantization: the
+// smallest S whose CTA count mtiles*S fills whole waves of 148 SMs to >= 90%
+// (at least one full wave), else the best fill up to 4 waves.  S depends on
+// (M, K) only -- never on the token count -- which keeps every token's
+// reduction order fixed.
+uint32_t* device_error_word();
+
 int choose_split(int M, int K) {
-    const int mtiles = M / kTileM;
+    const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
     const int KT = K / 16;
-    int S = (2 * 148 + mtiles / 2) / (mtiles > 0 ? mtiles : 1);
-    if (S < 1) S = 1;
-    const int max_s = KT / 8 > 0 ? KT / 8 : 1;
-    if (S > max_s) S = max_s;
-    return S;
+    const int max_s = KT / kChunkSteps > 0 ? (KT / kChunkSteps < 32 ? KT / kChunkSteps : 32) : 1;
+    constexpr int kSMs = 148;
+    int best = 1;
+    double best_eff = -1.0;
+    for (int S = 1; S <= max_s; ++S) {
+        const int ctas = mtiles * S;
+        const int waves = (ctas + kSMs - 1) / kSMs;
+        if (waves > 4 && best_eff >= 0.0) break;
+        const double eff = ctas < kSMs ? (double)ctas / kSMs : (double)ctas / ((double)waves * kSMs);
+        if (eff >= 0.9) return S;
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = S;
+        }
+    }
+    return best;
 }
 
 }  // namespace dkv
@@ -486,17 +584,17 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
         return DKV_OK;
     }
     const int nt = std::min(8, (std::min(N, 64) + 7) / 8);
-    const size_t smem_x = (size_t)2 * 8 * nt * kXStride * 2;
-    const size_t smem_t = (size_t)8 * nt * kTileStride * 4;
-    const size_t smem = std::max(smem_x, smem_t);
+    g.err = device_error_word();
+    // the result tile [NB][kTileStride] reuses the X staging buffers, which
+    // are larger, so the bf16 kernel's shared memory is gemm_smem<NT>()
 #define DKV_GEMM_CASE(NTV)                                                              \
     case NTV: {                                                                         \
         static bool attr = false;                                                       \
         if (!attr) {                                                                    \
-            DKV_CUDA(allow_smem(gemm_bf16_kernel<NTV>, 64 * 1024));                     \
+            DKV_CUDA(allow_smem_max(gemm_bf16_kernel<NTV>));                            \
             attr = true;                                                                \
         }                                                                               \
-        gemm_bf16_kernel<NTV><<<grid, 256, smem, st>>>(g);                              \
+        gemm_bf16_kernel<NTV><<<grid, 256, gemm_smem<NTV>(), st>>>(g);                  \
         break;                                                                          \
     }
     switch (nt) {

@@ -258,6 +258,16 @@ class CompressedKVCache:
     def _hwm_max(self) -> int:
         return int(self.meta_t[:, :, 0].max().item())
 
+    def _kept_after_fill(self, n: int, seen: int, layers) -> int:
+        """Entries a layer keeps after `n` rows are appended to it empty with
+        zero scores (the rebuild path writes only those)."""
+        most = 0
+        for L in layers:
+            c = self.cfgs[L]
+            budget = max(int(round(c.keep_frac * max(seen, 1))), c.sink + c.recent)
+            most = max(most, n if (n <= budget or c.recent <= 0) else budget)
+        return most
+
     # ---------------------------------------------------- protocol
     def append(self, layer: int, k, v, pos) -> None:
         """Quantize rows into free slots with score 0, then evict once
@@ -344,7 +354,7 @@ class CompressedKVCache:
             # everything is rewritten: clear, then refill every layer with the
             # rows that survive eviction at zero scores
             self.seen_t.zero_()
-            self._grow(n + 1)
+            self._grow(self._kept_after_fill(n, n, range(self.n_layers)) + 1)
             ctx = torch.full((self.batch,), n, dtype=torch.int32, device="cuda")
             layers = (C.c_int32 * self.n_layers)(*range(self.n_layers))
             _lib.call("dkv_comp_rebuild", self.struct(), full.struct(), self.dims(), layers, self.n_layers,
@@ -371,7 +381,8 @@ class CompressedKVCache:
         n = full.length
         if not self._ready:
             self.materialize(full.n_heads, full.d_head, full.dtype)
-        self._grow(n + 1)
+        seen = max(self.seen_positions, n) if 0 in layers else self.seen_positions
+        self._grow(self._kept_after_fill(n, seen, layers) + 1)
         ctx = torch.full((self.batch,), n, dtype=torch.int32, device="cuda")
         arr = (C.c_int32 * len(layers))(*layers)
         _lib.call("dkv_comp_rebuild", self.struct(), full.struct(), self.dims(), arr, len(layers),

@@ -240,15 +240,77 @@ def test_f32_gemm_matches_torch():
     torch.testing.assert_close(out, X @ W.t(), rtol=1e-5, atol=1e-4)
 
 
-# ------------------------------------------------------------- K3 / K2
+# ------------------------------------------------------------- K2
+@pytest.mark.parametrize("bits", [2, 3, 4, 8, 16])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_draft_attention_and_mass(bits, d, dtype):
+    """Drafter attention (T = 1) over the quantized slot cache vs a torch fp32
+    reference on the read-back (dequantized) entries, and the attention mass
+    folded into the slot scores (compress.py:144-151 + llama.py:213-216).
+    Tolerances: output 2e-2 of the output scale (f16 / bf16 operands), mass
+    1e-3 absolute + 3e-2 relative (bf16 queries of the 16-bit arm carry ~1%
+    probability error)."""
+    from draftkv import CompressedKVCache
+    L = lib()
+    B, n_kv, G, n = 2, 2, 4, 900
+    full_pages = -(-n // 16)
+    from draftkv import FullKVCache
+    full = FullKVCache(1, n_kv, d, dtype, capacity=n + 16, batch=B)
+    rng = np.random.default_rng(bits * 7 + d)
+    for b in range(B):
+        full.ensure(b, n)
+    k = round_bf16(rng.standard_normal((B, n, n_kv, d)).astype(np.float32))
+    v = round_bf16(rng.standard_normal((B, n, n_kv, d)).astype(np.float32))
+    src = torch.from_numpy(np.stack([k, v], axis=3)).to("cuda", torch.float32 if dtype == "f32" else torch.bfloat16)
+    p0 = torch.zeros((B,), dtype=torch.int32, device="cuda")
+    L.call("dkv_full_write", full.struct(), full.dims(), 0, src.data_ptr(), n, p0.data_ptr(), None, L.stream_ptr())
+    for b in range(B):
+        full.set_length(b, n)
+    comp = CompressedKVCache(1, CompressionConfig(bits, 0.5, 4, 32), n_kv=n_kv, d_head=d, dtype=dtype,
+                             capacity=n + 8, batch=B)
+    comp.sync_from(full, 0)
+    # give the slots distinct scores, then evict a few more through a resync
+    comp.score_t.copy_(torch.rand_like(comp.score_t))
+    q = torch.from_numpy(rng.standard_normal((B, n_kv * G, d)).astype(np.float32) * 2).cuda()
+    qpos = torch.full((B,), n, dtype=torch.int32, device="cuda")
+    out = torch.zeros((B, n_kv * G * d), dtype=torch.float32, device="cuda")
+    dims = comp.dims()
+    work = torch.zeros(int(L.load().dkv_attn_work_bytes(dims, G, 1, 16, 512, comp.cap)), dtype=torch.uint8,
+                       device="cuda")
+    before = comp.score_t.clone()
+    L.call("dkv_attn_comp", comp.struct(), dims, 0, G, q.data_ptr(), qpos.data_ptr(), out.data_ptr(), L.F32,
+           work.data_ptr(), work.numel(), L.stream_ptr())
+    after = comp.score_t.clone()
+    for b in range(B):
+        kk, vv, pp = comp.read(0, b)
+        pos_all = comp.pos_t[b, 0].cpu().numpy()
+        kt = torch.from_numpy(kk).cuda().repeat_interleave(G, dim=1)
+        vt = torch.from_numpy(vv).cuda().repeat_interleave(G, dim=1)
+        s = torch.einsum("hd,khd->hk", q[b], kt) / np.sqrt(d)
+        pr = torch.softmax(s, -1)
+        ref = torch.einsum("hk,khd->hd", pr, vt).reshape(-1)
+        scale = ref.abs().max().item()
+        assert (out[b] - ref).abs().max().item() <= 2e-2 * scale, b
+        mass = pr.reshape(n_kv, G, -1).sum(dim=(0, 1)).cpu().numpy()        # per live entry, position order
+        live = np.nonzero(pos_all >= 0)[0]
+        live = live[np.argsort(pos_all[live], kind="stable")]
+        got = (after[b, 0] - before[b, 0]).cpu().numpy()[live]
+        np.testing.assert_allclose(got, mass, atol=1e-3, rtol=3e-2)
+
+
+# ------------------------------------------------------------- K3
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("G", [1, 4])
-def test_full_attention_matches_torch_and_decode(dtype, G):
-    """Causal GQA attention over the paged cache vs a torch fp32 reference; the
-    T-row verify result equals T separate decode calls bit for bit."""
+@pytest.mark.parametrize("d", [64, 128])
+def test_full_attention_matches_torch_and_decode(dtype, G, d):
+    """Causal GQA attention over the paged cache vs a torch fp32 reference
+    (fp32 cache: 2e-5; bf16 cache through the tensor-core kernel, whose q and
+    p operands are bf16: 1e-2); the T-row verify result equals T separate
+    decode calls bit for bit."""
     from draftkv import PagedKVCache
     L = lib()
-    n_kv, d, n = 2, 64, 700
+    n_kv, n = 2, 700
     code = L.F32 if dtype == "f32" else L.BF16
     cache = PagedKVCache(1, n_kv, d, 16, 64, dtype, batch=1)
     rng = np.random.default_rng(G)
@@ -272,7 +334,8 @@ def test_full_attention_matches_torch_and_decode(dtype, G):
     mask = torch.arange(n, device="cuda")[None, :] > (p0 + torch.arange(T, device="cuda"))[:, None]
     s = s.masked_fill(mask[:, None, :], float("-inf"))
     ref = torch.einsum("qhk,khd->qhd", torch.softmax(s, -1), vv).reshape(T, -1)
-    torch.testing.assert_close(out, ref, rtol=2e-5, atol=2e-5)
+    tol = 2e-5 if dtype == "f32" else 1e-2
+    torch.testing.assert_close(out, ref, rtol=tol, atol=tol)
     for t in range(T):
         o1 = torch.zeros((1, n_kv * G * d), dtype=torch.float32, device="cuda")
         pt = torch.tensor([p0 + t], dtype=torch.int32, device="cuda")

@@ -613,3 +613,143 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     DKV_LAUNCHED();
     return DKV_OK;
 }
+
+// ---------------------------------------------------------------------------
+// dkv_gemm_noalloc: the same GEMM for callers that cannot allocate.
+//
+// Some callers cannot hand the library a work buffer: code that runs where
+// device allocation is unavailable or forbidden (inside an allocator hook or
+// an out-of-memory handler, a host that preallocated its whole HBM pool up
+// front, a plugin whose framework owns every allocation).  For them the
+// split-K partial tiles and the arrival tickets live in one fixed array
+// compiled into this library, so the call needs nothing but its inputs and
+// outputs.  The array costs DKV_GEMM_NOALLOC_SCRATCH_BYTES of device memory
+// on every GPU that loads the library, held until the process exits.
+//
+// The first call on a device does that device's set-up (finds the array's
+// device address and raises the kernels' shared-memory limit).  Make that
+// first call outside any stream capture.  Every call on a device shares the
+// one array: two calls whose kernels overlap on the GPU (different streams,
+// no ordering between them) race on it and give wrong results; calls on one
+// stream, or otherwise ordered, are safe.
+#include <mutex>
+
+namespace dkv {
+namespace {
+
+constexpr size_t kNoAllocBytes = DKV_GEMM_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kNoAllocTicketBytes = 16384;   // 4096 (row tile, token block) tickets
+constexpr int kNoAllocMaxDevices = 64;
+
+// In host code this name only stands for the device array; its device
+// address comes from cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_gemm_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+template <int NT>
+cudaError_t noalloc_attr() {
+    return allow_smem_max(gemm_bf16_kernel<NT>);
+}
+
+// Returns the current device's scratch address, doing the set-up on the first
+// call for that device.
+int noalloc_scratch(unsigned char** out) {
+    int dev = 0;
+    DKV_CUDA(cudaGetDevice(&dev));
+    DKV_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, "dkv_gemm_noalloc: device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        DKV_CUDA(cudaGetSymbolAddress(&p, g_gemm_noalloc_scratch));
+        DKV_REQUIRE(p && ((uintptr_t)p & 255) == 0, "dkv_gemm_noalloc: scratch array not 256-byte aligned");
+        DKV_CUDA(noalloc_attr<1>());
+        DKV_CUDA(noalloc_attr<2>());
+        DKV_CUDA(noalloc_attr<3>());
+        DKV_CUDA(noalloc_attr<4>());
+        DKV_CUDA(noalloc_attr<5>());
+        DKV_CUDA(noalloc_attr<6>());
+        DKV_CUDA(noalloc_attr<7>());
+        DKV_CUDA(noalloc_attr<8>());
+        g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return DKV_OK;
+}
+
+template <int NT>
+void noalloc_launch(const GemmArgs& g, dim3 grid, cudaStream_t st) {
+    gemm_bf16_kernel<NT><<<grid, 256, gemm_smem<NT>(), st>>>(g);
+}
+
+}  // namespace
+}  // namespace dkv
+
+extern "C" int dkv_gemm_noalloc(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K,
+                                const dkv_epilogue* epi, void* stream) {
+    DKV_REQUIRE(x && w && epi && M > 0 && N >= 0 && K > 0, "dkv_gemm_noalloc: bad arguments");
+    DKV_REQUIRE(x_dtype == w_dtype, "dkv_gemm_noalloc: x and w dtypes must match");
+    DKV_REQUIRE(w_dtype == DKV_BF16 || w_dtype == DKV_F32, "dkv_gemm_noalloc: dtype must be bf16 or f32");
+    DKV_REQUIRE(M % kTileM == 0, "dkv_gemm_noalloc: M (%d) must be padded to a multiple of 128", M);
+    DKV_REQUIRE(K % 16 == 0, "dkv_gemm_noalloc: K (%d) must be a multiple of 16", K);
+    int M_real = M;
+    if (epi->kind != DKV_EPI_QKV) {
+        DKV_REQUIRE(epi->ld_out > 0, "dkv_gemm_noalloc: ld_out required");
+        M_real = std::min(M, epi->ld_out);
+    } else {
+        DKV_REQUIRE(epi->q_out && epi->pos0 && epi->d_head > 0 && kTileM % epi->d_head == 0,
+                    "dkv_gemm_noalloc QKV: q_out/pos0 required and d_head must divide 128");
+        DKV_REQUIRE(epi->kv_stage || (epi->full && epi->full->k_pool), "dkv_gemm_noalloc QKV: no K/V destination");
+    }
+    if (N == 0) return DKV_OK;
+    const int mtiles = M / kTileM;
+    const int S = choose_split(M, K);
+    const int tok = w_dtype == DKV_F32 ? kF32Tok : 64;
+    const int nblk = (N + tok - 1) / tok;
+    const size_t tickets = (size_t)nblk * mtiles;
+    const size_t partial_bytes = S > 1 ? tickets * S * tok * kTileStride * sizeof(float) : 0;
+    DKV_REQUIRE(tickets * sizeof(unsigned) <= kNoAllocTicketBytes,
+                "dkv_gemm_noalloc: %zu row tiles x token blocks exceed the %zu tickets of the fixed scratch "
+                "(use dkv_gemm with a work buffer)", tickets, kNoAllocTicketBytes / sizeof(unsigned));
+    DKV_REQUIRE(partial_bytes <= kNoAllocBytes - kNoAllocTicketBytes,
+                "dkv_gemm_noalloc: M=%d N=%d K=%d needs %zu bytes of split-K scratch, the fixed array holds %zu "
+                "(use dkv_gemm with a work buffer)", M, N, K, partial_bytes, kNoAllocBytes - kNoAllocTicketBytes);
+    unsigned char* scratch = nullptr;
+    DKV_TRY(noalloc_scratch(&scratch));
+    cudaStream_t st = (cudaStream_t)stream;
+    // The array keeps whatever the previous call left; the tickets must start
+    // at zero (a launch that stopped early can leave one raised).
+    if (S > 1) DKV_CUDA(cudaMemsetAsync(scratch, 0, tickets * sizeof(unsigned), st));
+    GemmArgs g;
+    g.x = x;
+    g.w = w;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.S = S;
+    g.tickets = reinterpret_cast<unsigned*>(scratch);
+    g.ws = S > 1 ? reinterpret_cast<float*>(scratch + kNoAllocTicketBytes) : nullptr;
+    g.epi = make_epi(epi, M_real);
+    dim3 grid(mtiles * S, nblk);
+    if (w_dtype == DKV_F32) {
+        const size_t smem = std::max((size_t)kF32Tok * kF32Chunk * 4, (size_t)kF32Tok * kTileStride * 4);
+        gemm_f32_kernel<<<grid, 256, smem, st>>>(g);
+        DKV_LAUNCHED();
+        return DKV_OK;
+    }
+    g.err = device_error_word();
+    DKV_REQUIRE(g.err, "dkv_gemm_noalloc: device error word unavailable");
+    switch (std::min(8, (std::min(N, 64) + 7) / 8)) {
+        case 1: noalloc_launch<1>(g, grid, st); break;
+        case 2: noalloc_launch<2>(g, grid, st); break;
+        case 3: noalloc_launch<3>(g, grid, st); break;
+        case 4: noalloc_launch<4>(g, grid, st); break;
+        case 5: noalloc_launch<5>(g, grid, st); break;
+        case 6: noalloc_launch<6>(g, grid, st); break;
+        case 7: noalloc_launch<7>(g, grid, st); break;
+        default: noalloc_launch<8>(g, grid, st); break;
+    }
+    DKV_LAUNCHED();
+    return DKV_OK;
+}

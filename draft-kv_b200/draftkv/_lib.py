@@ -93,6 +93,8 @@ _SIGS = {
     "dkv_gemm": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(EpilogueS), vp,
                            C.c_size_t, vp]),
     "dkv_gemm_work_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "dkv_gemm_noalloc": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(EpilogueS),
+                                   vp]),
     "dkv_embed": (C.c_int, [vp, C.c_int, vp, vp, C.c_int, C.c_int, C.c_int, vp, C.c_int, C.c_int, C.c_int,
                             vp, vp]),
     "dkv_norm": (C.c_int, [vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_float, vp, C.c_int, vp]),

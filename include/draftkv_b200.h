@@ -234,6 +234,21 @@ DKV_API int dkv_gemm(const void* d_x, int x_dtype, const void* d_w, int w_dtype,
              const dkv_epilogue* epi, void* d_work, size_t work_bytes, void* stream);
 DKV_API size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype);
 
+/* dkv_gemm for callers that cannot allocate device memory: no counterpart in
+ * the reference (which has no native code).  Same arguments and results as
+ * dkv_gemm minus the work buffer; the split-K scratch is a fixed array of
+ * DKV_GEMM_NOALLOC_SCRATCH_BYTES compiled into the library, held on every
+ * GPU that loads it until the process exits.  Shapes whose split-K scratch
+ * exceeds it (e.g. M = 8192, K = 4096 at 64 tokens; 4096 x 4096, 4096 x 14336
+ * and the 128256-row head fit)
+ * return DKV_EINVAL with a message.
+ * Allocates nothing.  The first call on a device does that device's set-up;
+ * make it outside stream capture.  All calls on a device share the array:
+ * calls that overlap on the GPU race. */
+#define DKV_GEMM_NOALLOC_SCRATCH_BYTES (16u << 20)
+DKV_API int dkv_gemm_noalloc(const void* d_x, int x_dtype, const void* d_w, int w_dtype, int M, int N, int K,
+                             const dkv_epilogue* epi, void* stream);
+
 /* ------------------------------------------------------------ small ops */
 /* h[n] = emb[tok(n)] (+ pos_emb[pos0[b] + t]); tok(n) = tokens[b*tok_stride + t].
  * Replaces draftkv/gpt2.py:186 and draftkv/llama.py:180.  Ids outside

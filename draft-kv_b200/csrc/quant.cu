@@ -153,6 +153,199 @@ DKV_DEV void quant_pack_vector(const void* src, int src_dtype, size_t src_off, i
     __syncwarp();
 }
 
+// --------------------------------------------------------------------------
+// Lane-sliced quantize + pack (d % 64 == 0): each lane owns 16 consecutive
+// elements 16j..16j+15 of a vector (j = lane index within the vector's d/16
+// lanes), so a 64-element group is 4 neighbouring lanes and every packed
+// word is assembled in registers, OR-combined across the 2 or 4 lanes that
+// share it.  Same bytes as quant_pack_vector.
+//
+// Codes: q = clip(rint((x - lo) / scale)).  The quotient is first taken as
+// (x - lo) * RN(1/scale): its distance from the correctly rounded quotient is
+// below 4.6e-5 for quotients <= 255 (two fp32 roundings of relative 2^-24
+// each on the product, one on the quotient), so rint of the two agrees unless
+// the product lies within 1e-4 of a half-integer; only then is the IEEE
+// division evaluated.
+DKV_DEV void slice_group_params(const float (&x)[16], int bits, float* lo_out, float* scale_out) {
+    float lo = x[0], hi = x[0];
+#pragma unroll
+    for (int i = 1; i < 16; ++i) {
+        lo = fminf(lo, x[i]);
+        hi = fmaxf(hi, x[i]);
+    }
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 1));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 1));
+    lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 2));
+    hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 2));
+    const float levels = (float)((1 << bits) - 1);
+    *lo_out = lo;
+    *scale_out = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), levels), 1e-8f);
+}
+
+DKV_DEV uint32_t slice_code(float x, float lo, float scale, float rs, float qmax) {
+    const float num = __fsub_rn(x, lo);
+    const float t = __fmul_rn(num, rs);
+    float q = rintf(t);
+    if (fabsf(t - q) > 0.4999f) q = rintf(__fdiv_rn(num, scale));
+    q = fminf(fmaxf(q, 0.f), qmax);
+    return (uint32_t)q;
+}
+
+DKV_DEV void st_u32(uint8_t* p, uint32_t v) { *reinterpret_cast<uint32_t*>(p) = v; }
+
+// x: this lane's 16 elements (as f32); j: lane index within the vector.
+// Lanes of a warp must all call this together (shuffles); `active` = false
+// lanes compute on their (arbitrary) x and store nothing.  raw_dtype is the
+// storage dtype of 16-bit vectors.
+DKV_DEV void quant_pack_slice(const float (&x)[16], int j, int d, int bits, bool k_order, bool active,
+                              uint8_t* __restrict__ dst, uint16_t* __restrict__ dst_sl, int raw_dtype) {
+    const int q4 = d >> 2;     // elements (storage positions) per quad segment in K order
+    if (bits == 16) {
+        if (!active) return;
+        if (k_order) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int P = c * q4 + 4 * j;
+                store_from_f32(dst, raw_dtype, P + 0, x[2 * c]);
+                store_from_f32(dst, raw_dtype, P + 1, x[2 * c + 1]);
+                store_from_f32(dst, raw_dtype, P + 2, x[2 * c + 8]);
+                store_from_f32(dst, raw_dtype, P + 3, x[2 * c + 9]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) store_from_f32(dst, raw_dtype, 16 * j + i, x[i]);
+        }
+        return;
+    }
+    float lo, scale;
+    slice_group_params(x, bits, &lo, &scale);
+    const float rs = __frcp_rn(scale);
+    const float qmax = (float)((1 << bits) - 1);
+    uint32_t q[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) q[i] = slice_code(x[i], lo, scale, rs, qmax);
+    if (active && (j & 3) == 0) {
+        dst_sl[2 * (j >> 2)] = f32_to_half_bits(scale);
+        dst_sl[2 * (j >> 2) + 1] = f32_to_half_bits(lo);
+    }
+    if (!k_order) {
+        // element order: this lane owns whole words (2-bit: one word, 3-bit:
+        // one plane-A word and one plane-B unit, 4-bit: two words, 8-bit: four)
+        if (bits == 8) {
+            if (active) {
+#pragma unroll
+                for (int w = 0; w < 4; ++w)
+                    st_u32(dst + 16 * j + 4 * w, q[4 * w] | (q[4 * w + 1] << 8) | (q[4 * w + 2] << 16) | (q[4 * w + 3] << 24));
+            }
+        } else if (bits == 4) {
+            if (active) {
+#pragma unroll
+                for (int w = 0; w < 2; ++w) {
+                    uint32_t v = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) v |= (q[8 * w + 2 * i] << (4 * i)) | (q[8 * w + 2 * i + 1] << (16 + 4 * i));
+                    st_u32(dst + 8 * j + 4 * w, v);
+                }
+            }
+        } else {   // 2 or 3 bits: plane A in the 2-bit layout
+            uint32_t v = 0, u = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v |= ((q[2 * i] & 3u) << (2 * i)) | ((q[2 * i + 1] & 3u) << (16 + 2 * i));
+                u |= ((q[2 * i] >> 2) << i) | ((q[2 * i + 1] >> 2) << (8 + i));
+            }
+            if (active) {
+                st_u32(dst + 4 * j, v);
+                if (bits == 3) reinterpret_cast<uint16_t*>(dst + d / 4)[j] = (uint16_t)u;
+            }
+        }
+        return;
+    }
+    // fragment order: quad c's codes of this lane are elements 2c, 2c+1,
+    // 2c+8, 2c+9 at storage positions P = c*q4 + 4j + {0,1,2,3}
+    if (bits == 8) {
+        if (active) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                st_u32(dst + c * q4 + 4 * j, q[2 * c] | (q[2 * c + 1] << 8) | (q[2 * c + 8] << 16) | (q[2 * c + 9] << 24));
+        }
+    } else if (bits == 4) {
+        // a word holds 8 positions = lanes j (even) and j+1; position k of
+        // the word sits at bits 4*(k>>1) (+16 if k odd)
+        const int h = j & 1;
+        uint32_t piece[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            piece[c] = (q[2 * c] << (8 * h)) | (q[2 * c + 1] << (16 + 8 * h)) | (q[2 * c + 8] << (4 + 8 * h)) |
+                       (q[2 * c + 9] << (20 + 8 * h));
+            piece[c] |= __shfl_xor_sync(0xffffffffu, piece[c], 1);
+        }
+        if (active) {
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const int c = 2 * h + cc;
+                st_u32(dst + (c * q4 + 4 * (j & ~1)) / 2, piece[c]);
+            }
+        }
+    } else {   // 2 or 3 bits: a plane-A word / plane-B unit holds 16 positions = 4 lanes
+        const int m = j & 3;
+        uint32_t pa[4], pb[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint32_t a0 = q[2 * c], a1 = q[2 * c + 1], a2 = q[2 * c + 8], a3 = q[2 * c + 9];
+            pa[c] = ((a0 & 3u) << (4 * m)) | ((a1 & 3u) << (16 + 4 * m)) | ((a2 & 3u) << (4 * m + 2)) |
+                    ((a3 & 3u) << (18 + 4 * m));
+            pb[c] = ((a0 >> 2) << (2 * m)) | ((a1 >> 2) << (8 + 2 * m)) | ((a2 >> 2) << (2 * m + 1)) |
+                    ((a3 >> 2) << (9 + 2 * m));
+            pa[c] |= __shfl_xor_sync(0xffffffffu, pa[c], 1);
+            pa[c] |= __shfl_xor_sync(0xffffffffu, pa[c], 2);
+            if (bits == 3) {
+                pb[c] |= __shfl_xor_sync(0xffffffffu, pb[c], 1);
+                pb[c] |= __shfl_xor_sync(0xffffffffu, pb[c], 2);
+            }
+        }
+        if (active) {
+            uint32_t wa = pa[0], wb = pb[0];
+#pragma unroll
+            for (int c = 1; c < 4; ++c)
+                if (m == c) {
+                    wa = pa[c];
+                    wb = pb[c];
+                }
+            const int P = m * q4 + 4 * (j & ~3);      // first position of the word (quad c = m)
+            st_u32(dst + P / 4, wa);
+            if (bits == 3) reinterpret_cast<uint16_t*>(dst + d / 4)[P / 16] = (uint16_t)wb;
+        }
+    }
+}
+
+// Loads this lane's 16 elements (offset `off` + 16j of a row) as f32.
+DKV_DEV void load_slice(const void* src, int dtype, size_t off, float (&x)[16]) {
+    if (dtype == DKV_F32) {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(src) + off);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 v = __ldg(p + i);
+            x[4 * i] = v.x;
+            x[4 * i + 1] = v.y;
+            x[4 * i + 2] = v.z;
+            x[4 * i + 3] = v.w;
+        }
+    } else {
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(src) + off);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint4 v = __ldg(p + i);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                x[8 * i + 2 * k] = __uint_as_float(w[k] << 16);
+                x[8 * i + 2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+            }
+        }
+    }
+}
+
 // Dequantizes element e of a stored vector (test read-back path).
 DKV_DEV float dequant_elem(const uint8_t* codes, const uint16_t* sl, int d, int bits, bool k_order,
                            int e, int raw_dtype) {
@@ -189,16 +382,22 @@ DKV_DEV float dequant_elem(const uint8_t* codes, const uint16_t* sl, int d, int 
     return (float)q * scale + lo;
 }
 
-__global__ void quantize_pack_kernel(const void* src, int src_dtype, int64_t rows, int d, int bits,
-                                     bool k_order, uint8_t* codes, uint16_t* sl) {
-    extern __shared__ uint8_t qp_smem[];
-    const int warps = blockDim.x >> 5, wid = threadIdx.x >> 5;
-    const int64_t r = (int64_t)blockIdx.x * warps + wid;
-    if (r >= rows) return;
+// d % 64 == 0: d/16 lanes per row (lane-sliced packer).
+__global__ void quantize_pack_slice_kernel(const void* src, int src_dtype, int64_t rows, int d, int bits,
+                                           bool k_order, uint8_t* codes, uint16_t* sl) {
+    const int lpv = d >> 4, vpw = 32 / lpv;
+    const int lane = threadIdx.x & 31;
+    const int64_t base = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x - lane) / 32 * vpw;
+    const int64_t r = base + lane / lpv;
+    const int j = lane % lpv;
+    if (base >= rows) return;                 // uniform per warp
+    const bool active = r < rows;
+    const int64_t rr = active ? r : base;
     const int elem = src_dtype == DKV_F32 ? 4 : 2;
     const int cb = bits == 16 ? d * elem : d * bits / 8;
-    quant_pack_vector(src, src_dtype, (size_t)r * d, d, bits, k_order, codes + r * cb,
-                      sl + r * (d / 64) * 2, src_dtype, qp_smem + wid * d);
+    float x[16];
+    load_slice(src, src_dtype, (size_t)rr * d + 16 * j, x);
+    quant_pack_slice(x, j, d, bits, k_order, active, codes + rr * cb, sl + rr * (d / 64) * 2, src_dtype);
 }
 
 // --------------------------------------------------------------------------
@@ -685,6 +884,73 @@ __global__ void comp_rebuild_kernel(RebuildArgs a) {
     }
 }
 
+// Rebuild for d % 64 == 0: same plan and slot assignment as
+// comp_rebuild_kernel; vectors are quantized lane-sliced, d/16 lanes per
+// vector, consecutive vectors of a warp being consecutive slots of one
+// (head, K/V) so the loads stream whole rows of the paged cache.  Two vector
+// groups are loaded before either is packed.
+__global__ void __launch_bounds__(256) comp_rebuild_slice_kernel(RebuildArgs a) {
+    const int li = blockIdx.y, b = blockIdx.z;
+    const int L = a.layer_ids[li];
+    const CompView& c = a.c;
+    int kept, gap_at, gap_len, seen;
+    rebuild_plan(a, li, b, &kept, &gap_at, &gap_len, &seen);
+    const size_t bl = c.bl(b, L);
+    const int bits = a.cfg.bits[li];
+    if (kept > c.cap) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(a.err, 0x20u);
+        return;
+    }
+    const int r0 = blockIdx.x * a.rows_per_cta;
+    if (r0 >= c.cap) return;
+    const int r1 = min(r0 + a.rows_per_cta, c.cap);
+    for (int s = r0 + threadIdx.x; s < r1; s += blockDim.x) {
+        if (s < kept) {
+            c.pos[bl * c.cap + s] = s < gap_at ? s : s + gap_len;
+            c.score[bl * c.cap + s] = 0.f;
+        } else {
+            c.pos[bl * c.cap + s] = -1;
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        c.meta[bl * 4 + 0] = kept;
+        c.meta[bl * 4 + 1] = kept;
+    }
+    const int d = c.d, lpv = d >> 4, vpw = 32 / lpv;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int sub = lane / lpv, j = lane % lpv;
+    const int rq1 = min(r1, kept);
+    const int nslot = rq1 > r0 ? rq1 - r0 : 0;
+    const int n_vec = nslot * c.n_kv * 2;
+    const int sl_stride = (d / 64) * 2;
+    for (int base = wid * vpw; base < n_vec; base += 2 * nw * vpw) {     // uniform per warp
+        float x[2][16];
+        int vix[2];
+        bool act[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int v = base + u * nw * vpw + sub;
+            act[u] = v < n_vec;
+            vix[u] = act[u] ? v : base;
+            const int s = r0 + vix[u] % nslot, hk = vix[u] / nslot;
+            const bool is_k = hk < c.n_kv;
+            const int h = is_k ? hk : hk - c.n_kv;
+            const int p = s < gap_at ? s : s + gap_len;
+            load_slice(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, a.f.elem(b, L, h, p) + 16 * j, x[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (base + u * nw * vpw >= n_vec) break;           // uniform per warp
+            const int s = r0 + vix[u] % nslot, hk = vix[u] / nslot;
+            const bool is_k = hk < c.n_kv;
+            const int h = is_k ? hk : hk - c.n_kv;
+            const size_t vi = c.vec(b, L, h, s);
+            quant_pack_slice(x[u], j, d, bits, is_k, act[u], (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max,
+                             (is_k ? c.k_sl : c.v_sl) + vi * sl_stride, a.raw_dtype);
+        }
+    }
+}
+
 // seen update after a rebuild (one thread per sequence)
 __global__ void comp_seen_kernel(int32_t* seen, const int32_t* ctx, int batch, int advance, int trunc_zero) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -810,9 +1076,9 @@ extern "C" int dkv_quantize_pack(const void* src, int src_dtype, int64_t rows, i
     DKV_REQUIRE(d % 64 == 0 && d <= 256, "dkv_quantize_pack: d must be 64, 128 or 256 (got %d)", d);
     DKV_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 8 || bits == 16, "bad bits %d", bits);
     if (rows == 0) return DKV_OK;
-    const int warps = 8;
-    quantize_pack_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, warps * d,
-                           (cudaStream_t)stream>>>(src, src_dtype, rows, d, bits, k_order != 0, codes, sl);
+    const int rows_per_block = 8 * (32 / (d >> 4));     // 8 warps
+    quantize_pack_slice_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 256, 0,
+                                 (cudaStream_t)stream>>>(src, src_dtype, rows, d, bits, k_order != 0, codes, sl);
     DKV_LAUNCHED();
     return DKV_OK;
 }
@@ -906,7 +1172,10 @@ extern "C" int dkv_comp_rebuild(const dkv_comp_cache* comp, const dkv_full_cache
     dim3 grid((comp->cap + a.rows_per_cta - 1) / a.rows_per_cta, n_sel, dims.batch);
     {
         ProfScope ps(DKV_PROF_REBUILD, 0.0, (cudaStream_t)stream);
-        comp_rebuild_kernel<<<grid, warps * 32, warps * dims.d, (cudaStream_t)stream>>>(a);
+        if (dims.d % 64 == 0 && dims.d <= 512)
+            comp_rebuild_slice_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+        else
+            comp_rebuild_kernel<<<grid, warps * 32, warps * dims.d, (cudaStream_t)stream>>>(a);
     }
     DKV_LAUNCHED();
     // the layer-0 rebuild advances `seen` (compress.py:131-132); done after all

@@ -145,6 +145,39 @@ def test_sync_from_zero_keeps_the_reference_slots(cfg):
         assert np.abs(v - rv).max() <= 0.51 * (np.abs(rv).max() / ((1 << cfg.bits) - 1) if cfg.bits < 16 else 1e-6) + 1e-3
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("bits", [2, 3, 4, 8, 16])
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_rebuild_bytes_match_reference_packing(d, bits, dtype):
+    """The rebuild's codes, (scale, lo) and raw 16-bit vectors, byte for byte
+    against the reference quantizer packed in the storage order."""
+    n, n_kv = 150, 2
+    full, ref = _filled_full(n, n_kv=n_kv, d=d, seed=bits, dtype=dtype)
+    from draftkv import CompressedKVCache
+    comp = CompressedKVCache(2, CompressionConfig(bits, 1.0), n_kv=n_kv, d_head=d, dtype=dtype, capacity=256)
+    comp.sync_from(full, 0)
+    torch.cuda.synchronize()
+    for L in range(2):
+        rk, rv, _ = ref.read(L)                                    # [n][n_kv][d]
+        for name, x, k_order in (("k", rk, True), ("v", rv, False)):
+            codes = getattr(comp, name + "_codes")[0, L, :, :n].cpu().numpy()    # [n_kv][n][cb_max]
+            sl = getattr(comp, name + "_sl")[0, L, :, :n].cpu().numpy().view(np.float16)
+            for h in range(n_kv):
+                if bits == 16:
+                    order = oracle.quant.fragment_order(d) if k_order else np.arange(d)
+                    raw = np.ascontiguousarray(x[:, h, order], dtype=np.float32)
+                    want = (raw.astype(np.float32).view(np.uint8).reshape(n, -1) if dtype == "f32" else
+                            (raw.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)
+                            .reshape(n, -1))
+                    assert np.array_equal(codes[h][:, :want.shape[1]], want), (L, name, h)
+                    continue
+                rc, rs, rl, _ = oracle.quant_codes(x[:, h], bits)
+                want = oracle.pack_codes(rc[:, :d], bits, k_order=k_order)
+                assert np.array_equal(codes[h][:, :want.shape[1]], want), (L, name, h)
+                assert np.array_equal(sl[h][:, :, 0], rs.astype(np.float16)), (L, name, h)
+                assert np.array_equal(sl[h][:, :, 1], rl.astype(np.float16)), (L, name, h)
+
+
 def test_resync_rewrites_the_suffix():
     """Reference tests/test_lossless.py:60-77 on the device cache."""
     full, ref = _filled_full(120)

@@ -6,21 +6,30 @@
 // (draftkv/llama.py:213-216).
 //
 // One thread-block cluster of CS CTAs per (sequence, KV head); CTA r of the
-// cluster takes a contiguous 1/CS of the live slot range.  Its 8 warps walk
-// 16-slot tiles:
-//   S^T = Q K^T  with mma.m16n8k16: A = the group's queries (rows = heads,
-//                padded to 16), B = K read straight from the packed codes
-//                -- the K storage order puts each thread's fragment elements
-//                in one contiguous segment, so codes go register-direct to
-//                f16 (c, exact), and per group s = scale*S + lo*sum(q);
-//   O^T += V^T P^T  with V dequantized to f16 (c*scale + lo) in a per-warp
-//                swizzled shared tile read by ldmatrix.trans, and P from the
-//                S^T accumulators.
-// Raw scores stay in shared memory; after an online-softmax merge across the
-// warps, the cluster exchanges (max, sum) through distributed shared memory,
-// each CTA writes its share of the output and the exact attention mass of its
-// slots, and the last of the n_kv clusters to finish a slot range folds the
-// per-head masses into the slot scores in head order (atomic ticket, no wait).
+// cluster takes a contiguous 1/CS of the live slot range.  Each of its 8
+// warps walks 16-slot tiles through a private ring of NST shared-memory
+// stages filled by cp.async (NST-1 tiles in flight while one is consumed).
+//
+// Codes enter the tensor cores without dequantization.  One LOP3 (or PRMT)
+// turns a pair of codes into the f16 pair (1024 + f*c), exact, where f is a
+// power of two fixed by the pair's bit position (so no shift is needed to
+// align the field).  Then, per 64-group g of a slot:
+//   S = K Q^T   A = 16 slots of K in the fragment storage order, B = the
+//               group's queries scaled by 1/f (columns = heads, up to 8):
+//               sum_d q_d (1024 + f c_d)/f = sum_d q_d c_d + 1024 sum_d q_d/f,
+//               so s = scale_g (S_g - off_g) + lo_g sum_d q_d;
+//   O^T += X^T P'^T  X = the V pairs (1024 + f c) in a per-warp swizzled f16
+//               tile read by ldmatrix.trans, P'_g = p * vscale_g obtained
+//               from the S accumulators by movmatrix.trans, and at the end
+//               o_d = (acc_d - 1024 sum P'_g) / f_d + sum p * vlo_g.
+// 16-bit entries (raw bf16) take the plain path.  Scores are kept in log2
+// units (log2 e folded into the query scale) so the softmax uses exp2.
+// Raw scores stay in shared memory; after the warps' online-softmax states
+// are merged, the cluster exchanges (max, sum) through distributed shared
+// memory, each CTA writes its share of the output and the exact attention
+// mass of its slots, and the last of the n_kv clusters to finish a slot range
+// folds the per-head masses into the slot scores in head order (atomic
+// ticket, no wait).
 #include <cooperative_groups.h>
 
 #include "attn_common.cuh"
@@ -28,6 +37,8 @@
 namespace cg = cooperative_groups;
 
 namespace dkv {
+
+namespace {
 
 DKV_DEV uint32_t pk_f16(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
@@ -62,27 +73,31 @@ DKV_DEV void ldsm4t_(uint32_t (&r)[4], const void* p) {
                  : "r"(s));
 }
 
-// half2 of two integer codes (exact small integers).
-DKV_DEV uint32_t codes_to_h2(uint32_t pair_bits) {
-    const uint32_t biased = pair_bits | 0x64006400u;               // 1024 + c in each f16 lane
-    __half2 v = *reinterpret_cast<const __half2*>(&biased);
-    const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
-    v = __hsub2(v, k1024);
-    return *reinterpret_cast<uint32_t*>(&v);
+// Transpose of an 8x8 b16 matrix held one row-pair per thread.
+DKV_DEV uint32_t movm_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
 }
 
-// Code pair q (0-based, pairs of consecutive storage positions) of a packed
-// segment held in registers.  `w` holds the segment's 32-bit words; for 3 bits
-// `w` holds plane-A words and `u` plane-B 16-bit units.
-template <int BITS>
-DKV_DEV uint32_t pair_bits(const uint32_t* w, const uint16_t* u, int q) {
-    if (BITS == 4) return (w[q >> 2] >> (4 * (q & 3))) & 0x000F000Fu;
-    if (BITS == 2) return (w[q >> 3] >> (2 * (q & 7))) & 0x00030003u;
-    if (BITS == 8) {
-        const uint32_t x = w[q >> 1];
-        return (q & 1) ? (((x >> 16) & 0xFFu) | ((x >> 8) & 0xFF0000u)) : ((x & 0xFFu) | ((x << 8) & 0xFF0000u));
-    }
-    // 3 bits
+DKV_DEV void cpa16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+}
+DKV_DEV void cpa8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src));
+}
+DKV_DEV void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+DKV_DEV void cpa_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+DKV_DEV uint32_t h2_bits(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+DKV_DEV __half2 bits_h2(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+
+// Bits of code pair q (consecutive storage positions; the low half holds
+// the even position) of a 3-bit segment: plane-A words `w`, plane-B units `u`.
+DKV_DEV uint32_t pair_bits3(const uint32_t* w, const uint16_t* u, int q) {
     const uint32_t lo2 = (w[q >> 3] >> (2 * (q & 7))) & 0x00030003u;
     const uint32_t un = u[q >> 3];
     const uint32_t x = (un & 0xFFu) | ((un & 0xFF00u) << 8);
@@ -90,27 +105,74 @@ DKV_DEV uint32_t pair_bits(const uint32_t* w, const uint16_t* u, int q) {
     return lo2 | (hb << 2);
 }
 
+// Power-of-two factor f of code pair q: pair_x() yields 1024 + f*c.
+template <int BITS>
+DKV_DEV constexpr float pair_factor(int q) {
+    return BITS == 4 ? ((q & 1) ? 16.f : 1.f) : BITS == 2 ? (float)(1 << (2 * (q & 3))) : 1.f;
+}
+
+// f16 pair (1024 + f*c_even, 1024 + f*c_odd) of code pair q of a packed
+// segment held in registers (`w` its 32-bit words; 3 bits: plane-A words and
+// plane-B units `u`).  The pair layout puts pair i of a word at bit 2i*bits/2
+// of each half, so masking the field in place gives f = 2^(field offset).
+template <int BITS>
+DKV_DEV uint32_t pair_x(const uint32_t* w, const uint16_t* u, int q) {
+    if (BITS == 4) {
+        uint32_t x = w[q >> 2];
+        if (q & 2) x >>= 8;
+        return (x & ((q & 1) ? 0x00F000F0u : 0x000F000Fu)) | 0x64006400u;
+    }
+    if (BITS == 2) {
+        uint32_t x = w[q >> 3];
+        if (q & 4) x >>= 8;
+        return (x & (0x00030003u << (2 * (q & 3)))) | 0x64006400u;
+    }
+    if (BITS == 8) return __byte_perm(w[q >> 1], 0x64u, (q & 1) ? 0x4342 : 0x4140);
+    return pair_bits3(w, u, q) | 0x64006400u;
+}
+
+}  // namespace
+
 constexpr int kDraftWarps = 8;
 constexpr int kDraftThreads = kDraftWarps * 32;
+
+// Shared-memory stage of one 16-slot tile: K codes [16][KB], V codes [16][KB]
+// (16-bit entries: V rows in the swizzled order ldmatrix reads), K and V
+// (scale, lo) [16][NG][2] fp16, positions [16] int32.
+template <int D, int BITS>
+struct DraftGeo {
+    static constexpr bool RAW = BITS == 16;
+    static constexpr int KB = RAW ? D * 2 : D * BITS / 8;
+    static constexpr int NG = D / 64;
+    static constexpr int OFF_V = 16 * KB;
+    static constexpr int OFF_KSL = 32 * KB;
+    static constexpr int OFF_VSL = OFF_KSL + 16 * NG * 4;
+    static constexpr int OFF_POS = OFF_VSL + 16 * NG * 4;
+    static constexpr int STAGE = (OFF_POS + 64 + 127) / 128 * 128;
+    static constexpr int VT = RAW ? 0 : 16 * D * 2;     // per-warp f16 V tile
+};
 
 struct DraftArgs {
     AttnArgs a;
     int cs;                 // cluster size (CTAs per (sequence, head))
     int chunk_cap;          // slots per CTA the shared memory holds
+    int region;             // bytes of the stage rings + V tiles (or the epilogue's warp partials)
     int raw_dtype;          // dtype of 16-bit entries
+    int ch16;               // code rows are 16-byte aligned: 16-byte copies
     uint32_t* tickets;      // comp->tickets [batch][n_layers][64]
     uint32_t* err;
 };
 
-// Segment of quad c of a packed vector: bytes [c*D*BITS/32, ...), plus for 3
-// bits the plane-B units at D/4 + c*D/32.
+// This thread's K segment (quad c of slot row `row`) from a stage.
 template <int D, int BITS>
-DKV_DEV void load_k_segment(const uint8_t* vec, int c, uint32_t* w, uint16_t* u) {
+DKV_DEV void smem_k_segment(const uint8_t* kst, int row, int c, uint32_t* w, uint16_t* u) {
+    using Geo = DraftGeo<D, BITS>;
+    const uint8_t* vec = kst + row * Geo::KB;
     if (BITS == 16) {
         const uint4* p = reinterpret_cast<const uint4*>(vec + c * (D / 2));
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) {
-            const uint4 v = __ldg(p + i);
+            const uint4 v = p[i];
             w[4 * i] = v.x;
             w[4 * i + 1] = v.y;
             w[4 * i + 2] = v.z;
@@ -119,24 +181,58 @@ DKV_DEV void load_k_segment(const uint8_t* vec, int c, uint32_t* w, uint16_t* u)
     } else if (BITS == 3) {
         const uint32_t* pa = reinterpret_cast<const uint32_t*>(vec + c * (D / 16));
 #pragma unroll
-        for (int i = 0; i < D / 64; ++i) w[i] = __ldg(pa + i);
+        for (int i = 0; i < D / 64; ++i) w[i] = pa[i];
         const uint16_t* pb = reinterpret_cast<const uint16_t*>(vec + D / 4 + c * (D / 32));
 #pragma unroll
-        for (int i = 0; i < D / 64; ++i) u[i] = __ldg(pb + i);
+        for (int i = 0; i < D / 64; ++i) u[i] = pb[i];
     } else {
         constexpr int SEGB = D * BITS / 32;     // bytes per quad segment
         const uint32_t* p = reinterpret_cast<const uint32_t*>(vec + c * SEGB);
 #pragma unroll
-        for (int i = 0; i < SEGB / 4; ++i) w[i] = __ldg(p + i);
+        for (int i = 0; i < SEGB / 4; ++i) w[i] = p[i];
     }
 }
 
+// Stages this thread's share of V row `row` (elements [c*D/4, (c+1)*D/4)) as
+// the exact f16 values f*c into the warp's swizzled tile.
 template <int D, int BITS>
-__global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs da) {
-    constexpr bool RAW = BITS == 16;
+DKV_DEV void stage_v_row(const uint8_t* vst, int row, int c, uint16_t* vt) {
+    using Geo = DraftGeo<D, BITS>;
+    constexpr int EPQ = D / 4;                 // elements of this quad
+    const uint8_t* vv = vst + row * Geo::KB;
+    constexpr int SPAN = BITS == 3 ? EPQ / 4 : EPQ * BITS / 8;      // plane-A bytes for 3 bits
+    uint32_t w[SPAN / 4 > 0 ? SPAN / 4 : 1];
+    uint16_t u[EPQ / 16 > 0 ? EPQ / 16 : 1];
+    {
+        const uint8_t* p = vv + c * SPAN;
+#pragma unroll
+        for (int i = 0; i < SPAN / 4; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
+        if (BITS == 3) {
+            const uint16_t* pb = reinterpret_cast<const uint16_t*>(vv + D / 4) + c * (EPQ / 16);
+#pragma unroll
+            for (int i = 0; i < EPQ / 16; ++i) u[i] = pb[i];
+        }
+    }
+#pragma unroll
+    for (int c8 = 0; c8 < EPQ / 8; ++c8) {
+        const int chunk16 = (c * EPQ) / 8 + c8;
+        const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400u));
+        uint32_t o[4];
+#pragma unroll
+        for (int pi = 0; pi < 4; ++pi) o[pi] = h2_bits(__hsub2(bits_h2(pair_x<BITS>(w, u, c8 * 4 + pi)), k1024));
+        *reinterpret_cast<uint4*>(vt + row * D + ((chunk16 ^ (row & 7)) << 3)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+template <int D, int BITS, int NST>
+__global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftArgs da) {
+    using Geo = DraftGeo<D, BITS>;
+    constexpr bool RAW = Geo::RAW;
     constexpr int KS = D / 16;              // k16 steps over d
-    constexpr int NG = D / 64;              // quantization groups
+    constexpr int NG = Geo::NG;             // quantization groups
+    constexpr int KB = Geo::KB;
     constexpr int SEGW = RAW ? D / 8 : (BITS == 3 ? D / 64 : D * BITS / 128);   // words per quad segment
+    constexpr float kLog2e = 1.4426950408889634f;
     const AttnArgs& a = da.a;
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
@@ -152,230 +248,278 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
     const int s0 = min(rank * chunk, hwm), s1 = min(s0 + chunk, hwm);
     const int qpos = a.qpos0[b];
     const int HQ = a.n_kv * G;
+    const int cc = da.chunk_cap;
 
     extern __shared__ __align__(128) uint8_t dsm[];
-    float* sbuf = reinterpret_cast<float*>(dsm);                            // [G][chunk_cap]
-    uint16_t* vtile = reinterpret_cast<uint16_t*>(sbuf + (size_t)G * da.chunk_cap);   // [warps][16][D]
-    float* cta_m = reinterpret_cast<float*>(vtile + kDraftWarps * 16 * D);  // [8]
+    uint8_t* ring = dsm + (size_t)warp * NST * Geo::STAGE;
+    uint16_t* vt = reinterpret_cast<uint16_t*>(dsm + (size_t)kDraftWarps * NST * Geo::STAGE) + warp * 16 * D;
+    float* sbuf = reinterpret_cast<float*>(dsm + da.region);                // [G][chunk_cap], log2 units
+    float* cta_m = sbuf + (size_t)G * cc;                                   // [8]
     float* cta_l = cta_m + 8;                                               // [8]
     float* cta_o = cta_l + 8;                                               // [8][D]
     float* glob_m = cta_o + 8 * D;                                          // [8]
     float* glob_l = glob_m + 8;                                             // [8]
-    uint16_t* vt = vtile + warp * 16 * D;
 
-    if (chunk > da.chunk_cap) {       // host sized the launch; never expected
+    if (chunk > cc) {       // host sized the launch; never expected
         if (threadIdx.x == 0) atomicOr(da.err, 0x40u);
     }
 
-    // ---- queries of head qr (rows >= G and the upper 8 rows are zero)
+    const size_t vh = (bl * a.n_kv + h) * (size_t)src.cap;       // first vector of (b, layer, head)
+    const uint8_t* kbase = src.k_codes + vh * src.cb_max;
+    const uint8_t* vbase = src.v_codes + vh * src.cb_max;
+    const uint8_t* kslb = reinterpret_cast<const uint8_t*>(src.k_sl + vh * NG * 2);
+    const uint8_t* vslb = reinterpret_cast<const uint8_t*>(src.v_sl + vh * NG * 2);
+    const uint8_t* posb = reinterpret_cast<const uint8_t*>(src.cpos + bl * src.cap);
+
+    const int first_tile = s0 / 16;
+    const int n_tiles = s1 > s0 ? (s1 - 1) / 16 - first_tile + 1 : 0;
+    const int my_n = n_tiles > warp ? (n_tiles - 1 - warp) / kDraftWarps + 1 : 0;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+
+    // this lane's copy chunks of a tile: code chunk k is row ck / CPR, column
+    // ck % CPR with ck = lane + 32k; one (scale, lo) or position chunk
+    constexpr int CW = (KB % 16 == 0) ? 16 : 8;
+    const int cw = (CW == 16 && (RAW || da.ch16)) ? 16 : 8;
+    const int cpr = KB / cw;
+    constexpr int MAXC = (16 * KB / 8 + 31) / 32;
+    const int nck = (16 * cpr + 31) / 32;
+    constexpr int SLC = NG * 4;      // 16-byte chunks of one (scale, lo) tile
+    const uint8_t* aux_src = lane < SLC ? kslb : lane < 2 * SLC ? vslb : posb;
+    const int aux_el = lane < 2 * SLC ? NG * 4 : 4;            // bytes per slot of that array
+    const int aux_off = (lane < SLC ? lane : lane < 2 * SLC ? lane - SLC : lane - 2 * SLC) * 16;
+    const uint32_t aux_dst = (lane < SLC ? Geo::OFF_KSL : lane < 2 * SLC ? Geo::OFF_VSL : Geo::OFF_POS) + aux_off;
+    const bool aux_on = lane < 2 * SLC + 4;
+
+    // per chunk: global offset from the tile's first row, K and V stage offsets
+    int c_go[MAXC], c_ko[MAXC], c_vo[MAXC];
+#pragma unroll
+    for (int k = 0; k < MAXC; ++k) {
+        const int ck = lane + 32 * k;
+        c_go[k] = -1;
+        if (k < nck && ck < 16 * cpr) {
+            const int row = cw == 16 ? ck / (KB / 16 > 0 ? KB / 16 : 1) : ck / (KB / 8);
+            const int col = cw == 16 ? ck % (KB / 16 > 0 ? KB / 16 : 1) : ck % (KB / 8);
+            c_go[k] = row * src.cb_max + col * cw;
+            c_ko[k] = row * KB + col * cw;
+            c_vo[k] = Geo::OFF_V + row * KB + (RAW ? ((col ^ (row & 7)) * 16) : col * cw);
+        }
+    }
+
+    auto issue = [&](int i) {
+        if (i < my_n) {
+            const int base = (first_tile + warp + i * kDraftWarps) * 16;
+            const uint32_t st = ring_s + (uint32_t)((i % NST) * Geo::STAGE);
+            const uint8_t* kt = kbase + (size_t)base * src.cb_max;
+            const uint8_t* vtile = vbase + (size_t)base * src.cb_max;
+#pragma unroll
+            for (int k = 0; k < MAXC; ++k) {
+                if (c_go[k] >= 0) {
+                    if (CW == 16 && cw == 16) {
+                        cpa16(st + c_ko[k], kt + c_go[k]);
+                        cpa16(st + c_vo[k], vtile + c_go[k]);
+                    } else {
+                        cpa8(st + c_ko[k], kt + c_go[k]);
+                        cpa8(st + c_vo[k], vtile + c_go[k]);
+                    }
+                }
+            }
+            if (aux_on) cpa16(st + aux_dst, aux_src + (size_t)base * aux_el + aux_off);
+        }
+        cpa_commit();
+    };
+
+#pragma unroll
+    for (int i = 0; i < NST - 1; ++i) issue(i);
+
+    // ---- queries as the B operand: column = head qr (heads >= G are zero),
+    // scaled by 1/sqrt(d) * log2(e) and, per code pair, by 1/f
     const bool qrow = qr < G;
     const float* qv = a.q + ((size_t)b * HQ + h * G + (qrow ? qr : 0)) * D;
-    uint32_t qa[KS][4];
-    float qsum[NG] = {};
+    const float qscale = a.scale * kLog2e;
+    uint32_t qb[KS][2];
+    float qsum[NG] = {}, qoff[NG] = {};
 #pragma unroll
     for (int kk = 0; kk < KS; ++kk) {
         const int d0 = kk * 16 + 2 * qc;
         float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
         if (qrow) {
-            x0 = qv[d0] * a.scale;
-            x1 = qv[d0 + 1] * a.scale;
-            x2 = qv[d0 + 8] * a.scale;
-            x3 = qv[d0 + 9] * a.scale;
+            x0 = qv[d0] * qscale;
+            x1 = qv[d0 + 1] * qscale;
+            x2 = qv[d0 + 8] * qscale;
+            x3 = qv[d0 + 9] * qscale;
         }
-        if (RAW && src.dtype == DKV_BF16) {
-            qa[kk][0] = pk_bf16(x0, x1);
-            qa[kk][2] = pk_bf16(x2, x3);
+        if constexpr (RAW) {
+            qb[kk][0] = pk_bf16(x0, x1);
+            qb[kk][1] = pk_bf16(x2, x3);
         } else {
-            qa[kk][0] = pk_f16(x0, x1);
-            qa[kk][2] = pk_f16(x2, x3);
-            // sum of the f16-rounded scaled queries per group (for the lo term)
-            const __half2 h01 = *reinterpret_cast<__half2*>(&qa[kk][0]);
-            const __half2 h23 = *reinterpret_cast<__half2*>(&qa[kk][2]);
+            // the f16-rounded query values q; pair 2kk multiplies d0, d0+1 and
+            // pair 2kk+1 multiplies d0+8, d0+9 (exact power-of-two rescale)
+            const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
+            const float f0 = pair_factor<BITS>(2 * kk), f1 = pair_factor<BITS>(2 * kk + 1);
+            const __half2 s01 = __hmul2(h01, __float2half2_rn(1.f / f0));
+            const __half2 s23 = __hmul2(h23, __float2half2_rn(1.f / f1));
+            qb[kk][0] = *reinterpret_cast<const uint32_t*>(&s01);
+            qb[kk][1] = *reinterpret_cast<const uint32_t*>(&s23);
             qsum[kk / 4] += __low2float(h01) + __high2float(h01) + __low2float(h23) + __high2float(h23);
+            qoff[kk / 4] += 1024.f * (__low2float(s01) + __high2float(s01) + __low2float(s23) + __high2float(s23));
         }
-        qa[kk][1] = 0u;
-        qa[kk][3] = 0u;
     }
+    // per head qr, then fetched for this thread's S columns (heads 2qc, 2qc+1)
+    float qs0[NG], qs1[NG], qo0[NG], qo1[NG];
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
         qsum[g] += __shfl_xor_sync(0xffffffffu, qsum[g], 1);
         qsum[g] += __shfl_xor_sync(0xffffffffu, qsum[g], 2);
+        qoff[g] += __shfl_xor_sync(0xffffffffu, qoff[g], 1);
+        qoff[g] += __shfl_xor_sync(0xffffffffu, qoff[g], 2);
+        qs0[g] = __shfl_sync(0xffffffffu, qsum[g], 8 * qc);
+        qs1[g] = __shfl_sync(0xffffffffu, qsum[g], 8 * qc + 4);
+        qo0[g] = __shfl_sync(0xffffffffu, qoff[g], 8 * qc);
+        qo1[g] = __shfl_sync(0xffffffffu, qoff[g], 8 * qc + 4);
     }
 
-    float m_run = -INFINITY, l_run = 0.f;    // stats of head qr
+    // online-softmax maxima of heads 2qc (0) and 2qc+1 (1); the sums come
+    // from an extra product per tile: C2 = A2 P^T with A2 rows g < NG = vlo_g
+    // of the slots and row NG = ones, so C2 row g = sum p * vlo_g and row NG =
+    // sum p (16-bit entries: row 0 = sum p)
+    constexpr int ROW1 = RAW ? 0 : NG;
+    float m0 = -INFINITY, m1 = -INFINITY;
+    float c2[4] = {0.f, 0.f, 0.f, 0.f};
     float oacc[KS][4];                       // O^T: rows d = 16md + qr (+8), cols heads 2qc, 2qc+1
 #pragma unroll
     for (int md = 0; md < KS; ++md) oacc[md][0] = oacc[md][1] = oacc[md][2] = oacc[md][3] = 0.f;
 
-    const uint8_t* kbase = src.k_codes + (bl * a.n_kv + h) * (size_t)src.cap * src.cb_max;
-    const uint8_t* vbase = src.v_codes + (bl * a.n_kv + h) * (size_t)src.cap * src.cb_max;
-    const uint16_t* ksl = src.k_sl + (bl * a.n_kv + h) * (size_t)src.cap * NG * 2;
-    const uint16_t* vsl = src.v_sl + (bl * a.n_kv + h) * (size_t)src.cap * NG * 2;
-    const int32_t* cpos = src.cpos + bl * src.cap;
 
-    const int first_tile = s0 / 16;
-    const int n_tiles = s1 > s0 ? (s1 - 1) / 16 - first_tile + 1 : 0;
-    for (int tt = warp; tt < n_tiles; tt += kDraftWarps) {
-        const int base = (first_tile + tt) * 16;
-        // ---- K: register-direct B fragments of slots base+qr and base+8+qr
-        float sc[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+    for (int it = 0; it < my_n; ++it) {
+        issue(it + NST - 1);
+        cpa_wait<NST - 1>();
+        __syncwarp();
+        const uint8_t* st = ring + (it % NST) * Geo::STAGE;
+        const int base = (first_tile + warp + it * kDraftWarps) * 16;
+
+        // ---- S = K Q^T: rows slots qr / qr+8, columns heads 2qc / 2qc+1
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
         {
             uint32_t w0[SEGW > 0 ? SEGW : 1], w1[SEGW > 0 ? SEGW : 1];
             uint16_t u0[D / 64 > 0 ? D / 64 : 1], u1[D / 64 > 0 ? D / 64 : 1];
-            const int sa = base + qr, sb = base + 8 + qr;
-            load_k_segment<D, BITS>(kbase + (size_t)min(sa, src.cap - 1) * src.cb_max, qc, w0, u0);
-            load_k_segment<D, BITS>(kbase + (size_t)min(sb, src.cap - 1) * src.cb_max, qc, w1, u1);
-            if (RAW) {
+            smem_k_segment<D, BITS>(st, qr, qc, w0, u0);
+            smem_k_segment<D, BITS>(st, qr + 8, qc, w1, u1);
+            if constexpr (RAW) {
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
-                    mma16816<true>(sc[0], qa[kk], w0[2 * kk], w0[2 * kk + 1]);
-                    mma16816<true>(sc[1], qa[kk], w1[2 * kk], w1[2 * kk + 1]);
+                    const uint32_t af[4] = {w0[2 * kk], w1[2 * kk], w0[2 * kk + 1], w1[2 * kk + 1]};
+                    mma16816<true>(sc, af, qb[kk][0], qb[kk][1]);
                 }
             } else {
-                float gs[NG][2][4];
+                float gs[NG][4];
 #pragma unroll
-                for (int g = 0; g < NG; ++g)
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) gs[g][nt][0] = gs[g][nt][1] = gs[g][nt][2] = gs[g][nt][3] = 0.f;
+                for (int g = 0; g < NG; ++g) gs[g][0] = gs[g][1] = gs[g][2] = gs[g][3] = 0.f;
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
-                    const uint32_t b00 = codes_to_h2(pair_bits<BITS>(w0, u0, 2 * kk));
-                    const uint32_t b01 = codes_to_h2(pair_bits<BITS>(w0, u0, 2 * kk + 1));
-                    const uint32_t b10 = codes_to_h2(pair_bits<BITS>(w1, u1, 2 * kk));
-                    const uint32_t b11 = codes_to_h2(pair_bits<BITS>(w1, u1, 2 * kk + 1));
-                    mma16816<false>(gs[kk / 4][0], qa[kk], b00, b01);
-                    mma16816<false>(gs[kk / 4][1], qa[kk], b10, b11);
+                    const uint32_t af[4] = {pair_x<BITS>(w0, u0, 2 * kk), pair_x<BITS>(w1, u1, 2 * kk),
+                                            pair_x<BITS>(w0, u0, 2 * kk + 1), pair_x<BITS>(w1, u1, 2 * kk + 1)};
+                    mma16816<false>(gs[kk / 4], af, qb[kk][0], qb[kk][1]);
                 }
-                // per-slot group scale / lo: this thread's columns are slots
-                // base + 8nt + 2qc (+1)
+                const uint32_t* ksl = reinterpret_cast<const uint32_t*>(st + Geo::OFF_KSL);
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int sl = base + 8 * nt + 2 * qc;
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = hr ? qr + 8 : qr;
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int slot = min(sl + e, src.cap - 1);
-                        float acc = 0.f;
-#pragma unroll
-                        for (int g = 0; g < NG; ++g) {
-                            const float scl = half_bits_to_f32(__ldg(ksl + ((size_t)slot * NG + g) * 2));
-                            const float lo = half_bits_to_f32(__ldg(ksl + ((size_t)slot * NG + g) * 2 + 1));
-                            acc += scl * gs[g][nt][e] + lo * qsum[g];
-                        }
-                        sc[nt][e] = acc;
+                    for (int g = 0; g < NG; ++g) {
+                        const uint32_t slw = ksl[row * NG + g];
+                        const float2 sl2 = __half22float2(bits_h2(slw));
+                        const float scl = sl2.x, lo = sl2.y;
+                        sc[2 * hr] += scl * (gs[g][2 * hr] - qo0[g]) + lo * qs0[g];
+                        sc[2 * hr + 1] += scl * (gs[g][2 * hr + 1] - qo1[g]) + lo * qs1[g];
                     }
                 }
             }
         }
         // ---- mask (empty slot, outside this CTA's range, future position)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int slot = base + 8 * nt + 2 * qc + e;
-                bool ok = slot >= s0 && slot < s1 && qrow;
-                if (ok) {
-                    const int p = __ldg(cpos + slot);
-                    ok = p >= 0 && p <= qpos;
-                }
-                if (!ok) sc[nt][e] = -INFINITY;
-                if (qrow && slot >= s0 && slot < s1 && slot - s0 < da.chunk_cap)
-                    sbuf[(size_t)qr * da.chunk_cap + (slot - s0)] = sc[nt][e];
-            }
-        // ---- online softmax for head qr
-        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float nm = fmaxf(m_run, mx);
-        const float alpha = nm == -INFINITY ? 1.f : expf(m_run - nm);
-        float p[2][2];
-        float psum = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                p[nt][e] = sc[nt][e] == -INFINITY ? 0.f : expf(sc[nt][e] - nm);
-                psum += p[nt][e];
-            }
-        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-        l_run = l_run * alpha + psum;
-        m_run = nm;
-        // rescale O^T columns (heads 2qc, 2qc+1): their alphas live in lanes 8qc and 8qc+4
-        const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * qc);
-        const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * qc + 4);
-#pragma unroll
-        for (int md = 0; md < KS; ++md) {
-            oacc[md][0] *= al0;
-            oacc[md][1] *= al1;
-            oacc[md][2] *= al0;
-            oacc[md][3] *= al1;
-        }
-        // ---- V tile (16 slots x D) dequantized into this warp's shared tile
+        const int32_t* ps = reinterpret_cast<const int32_t*>(st + Geo::OFF_POS);
+        const int sa = base + qr, sb = base + 8 + qr;
+        const bool ina = sa >= s0 && sa < s1, inb = sb >= s0 && sb < s1;
+        const int pa = ps[qr], pb = ps[qr + 8];
+        if (!(ina && pa >= 0 && pa <= qpos)) sc[0] = sc[1] = -INFINITY;
+        if (!(inb && pb >= 0 && pb <= qpos)) sc[2] = sc[3] = -INFINITY;
         {
-            const int slot_a = base + qr, slot_b = base + 8 + qr;
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int row = qr + 8 * half;
-                const int slot = min(half ? slot_b : slot_a, src.cap - 1);
-                const uint8_t* vv = vbase + (size_t)slot * src.cb_max;
-                constexpr int EPQ = D / 4;            // elements of this quad
-#pragma unroll
-                for (int c8 = 0; c8 < EPQ / 8; ++c8) {
-                    const int e0 = qc * EPQ + c8 * 8;     // first element of this 16-byte chunk
-                    uint4 out;
-                    if (RAW) {
-                        out = __ldg(reinterpret_cast<const uint4*>(vv + e0 * 2));
-                    } else {
-                        const int g = e0 / 64;
-                        const float scl = half_bits_to_f32(__ldg(vsl + ((size_t)slot * NG + g) * 2));
-                        const float lo = half_bits_to_f32(__ldg(vsl + ((size_t)slot * NG + g) * 2 + 1));
-                        uint32_t wv[2] = {0u, 0u};
-                        uint16_t uv[1] = {0};
-                        float f[8];
-                        if (BITS == 4) {
-                            wv[0] = __ldg(reinterpret_cast<const uint32_t*>(vv + e0 / 2));
-                        } else if (BITS == 8) {
-                            const uint2 t = __ldg(reinterpret_cast<const uint2*>(vv + e0));
-                            wv[0] = t.x;
-                            wv[1] = t.y;
-                        } else if (BITS == 2) {
-                            // one word holds 16 codes; elements e0..e0+7 are its pairs (e0%16)/2 .. +3
-                            wv[0] = __ldg(reinterpret_cast<const uint32_t*>(vv + (e0 / 16) * 4));
-                        } else {  // 3 bit
-                            wv[0] = __ldg(reinterpret_cast<const uint32_t*>(vv + (e0 / 16) * 4));
-                            uv[0] = __ldg(reinterpret_cast<const uint16_t*>(vv + D / 4 + (e0 / 16) * 2));
-                        }
-#pragma unroll
-                        for (int pi = 0; pi < 4; ++pi) {
-                            uint32_t bits;
-                            if (BITS == 4) bits = pair_bits<4>(wv, uv, pi);
-                            else if (BITS == 8) bits = pair_bits<8>(wv, uv, pi);
-                            else if (BITS == 2) bits = pair_bits<2>(wv, uv, ((e0 % 16) / 2) + pi);
-                            else bits = pair_bits<3>(wv, uv, ((e0 % 16) / 2) + pi);
-                            f[2 * pi] = (float)(bits & 0xFFFFu);
-                            f[2 * pi + 1] = (float)(bits >> 16);
-                        }
-                        out.x = pk_f16(f[0] * scl + lo, f[1] * scl + lo);
-                        out.y = pk_f16(f[2] * scl + lo, f[3] * scl + lo);
-                        out.z = pk_f16(f[4] * scl + lo, f[5] * scl + lo);
-                        out.w = pk_f16(f[6] * scl + lo, f[7] * scl + lo);
-                    }
-                    const int chunk16 = e0 / 8;
-                    *reinterpret_cast<uint4*>(vt + row * D + ((chunk16 ^ (row & 7)) << 3)) = out;
-                }
+            const int h0 = 2 * qc, h1 = 2 * qc + 1;
+            if (ina && sa - s0 < cc) {
+                if (h0 < G) sbuf[(size_t)h0 * cc + (sa - s0)] = sc[0];
+                if (h1 < G) sbuf[(size_t)h1 * cc + (sa - s0)] = sc[1];
+            }
+            if (inb && sb - s0 < cc) {
+                if (h0 < G) sbuf[(size_t)h0 * cc + (sb - s0)] = sc[2];
+                if (h1 < G) sbuf[(size_t)h1 * cc + (sb - s0)] = sc[3];
             }
         }
-        __syncwarp();
-        // ---- O^T += V^T P^T
-        uint32_t pb0, pb1;
-        if (RAW && src.dtype == DKV_BF16) {
-            pb0 = pk_bf16(p[0][0], p[0][1]);
-            pb1 = pk_bf16(p[1][0], p[1][1]);
+        // ---- online softmax (base 2) of the two heads over the tile's 16 slots
+        float t0 = fmaxf(sc[0], sc[2]), t1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            t0 = fmaxf(t0, __shfl_xor_sync(0xffffffffu, t0, off));
+            t1 = fmaxf(t1, __shfl_xor_sync(0xffffffffu, t1, off));
+        }
+        {
+            const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
+            if (!__all_sync(0xffffffffu, n0 == m0 && n1 == m1)) {
+                const float al0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
+                const float al1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+#pragma unroll
+                for (int md = 0; md < KS; ++md) {
+                    oacc[md][0] *= al0;
+                    oacc[md][1] *= al1;
+                    oacc[md][2] *= al0;
+                    oacc[md][3] *= al1;
+                }
+                c2[0] *= al0;
+                c2[1] *= al1;
+                m0 = n0;
+                m1 = n1;
+            }
+        }
+        // p (f16): slot qr -> pa2 (heads 2qc, 2qc+1), slot qr+8 -> pb2
+        const float e0 = m0 == -INFINITY ? -INFINITY : sc[0] - m0;
+        const float e1 = m1 == -INFINITY ? -INFINITY : sc[1] - m1;
+        const float e2 = m0 == -INFINITY ? -INFINITY : sc[2] - m0;
+        const float e3 = m1 == -INFINITY ? -INFINITY : sc[3] - m1;
+        const __half2 pa2 = __floats2half2_rn(exp2f(e0), exp2f(e1));
+        const __half2 pb2 = __floats2half2_rn(exp2f(e2), exp2f(e3));
+        // ---- sums: C2 += A2 P^T
+        {
+            uint32_t a2[4] = {0u, 0u, 0u, 0u};
+            if constexpr (!RAW) {
+                if (qr < NG) {
+                    const uint32_t* vsl = reinterpret_cast<const uint32_t*>(st + Geo::OFF_VSL);
+                    a2[0] = __byte_perm(vsl[(2 * qc) * NG + qr], vsl[(2 * qc + 1) * NG + qr], 0x7632);
+                    a2[2] = __byte_perm(vsl[(2 * qc + 8) * NG + qr], vsl[(2 * qc + 9) * NG + qr], 0x7632);
+                }
+            }
+            if (qr == ROW1) a2[0] = a2[2] = 0x3C003C00u;     // f16 ones
+            mma16816<false>(c2, a2, movm_t(h2_bits(pa2)), movm_t(h2_bits(pb2)));
+        }
+        // ---- P'^T fragments (B of O^T += X^T P'^T)
+        uint32_t pbf[NG][2];
+        const uint16_t* vsrc;
+        if constexpr (RAW) {
+            // bf16 entries: P in bf16
+            const float2 fa = __half22float2(pa2), fb = __half22float2(pb2);
+            pbf[0][0] = movm_t(pk_bf16(fa.x, fa.y));
+            pbf[0][1] = movm_t(pk_bf16(fb.x, fb.y));
+            vsrc = reinterpret_cast<const uint16_t*>(st + Geo::OFF_V);
         } else {
-            pb0 = pk_f16(p[0][0], p[0][1]);
-            pb1 = pk_f16(p[1][0], p[1][1]);
+            const uint32_t* vsl = reinterpret_cast<const uint32_t*>(st + Geo::OFF_VSL);
+#pragma unroll
+            for (int g = 0; g < NG; ++g) {
+                const __half2 sa2 = bits_h2(__byte_perm(vsl[qr * NG + g], 0u, 0x1010));
+                const __half2 sb2 = bits_h2(__byte_perm(vsl[(qr + 8) * NG + g], 0u, 0x1010));
+                pbf[g][0] = movm_t(h2_bits(__hmul2(pa2, sa2)));
+                pbf[g][1] = movm_t(h2_bits(__hmul2(pb2, sb2)));
+            }
+            stage_v_row<D, BITS>(st + Geo::OFF_V, qr, qc, vt);
+            stage_v_row<D, BITS>(st + Geo::OFF_V, qr + 8, qc, vt);
+            __syncwarp();
+            vsrc = vt;
         }
         {
             const int mi = lane >> 3, ri = lane & 7;
@@ -383,23 +527,46 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
             for (int md = 0; md < KS; ++md) {
                 uint32_t va[4];
                 const int row = (mi >> 1) * 8 + ri;
-                ldsm4t_(va, vt + row * D + (((2 * md + (mi & 1)) ^ (row & 7)) << 3));
-                if (RAW && src.dtype == DKV_BF16)
-                    mma16816<true>(oacc[md], va, pb0, pb1);
-                else
-                    mma16816<false>(oacc[md], va, pb0, pb1);
+                ldsm4t_(va, vsrc + row * D + (((2 * md + (mi & 1)) ^ (row & 7)) << 3));
+                const int g = RAW ? 0 : md / 4;
+                mma16816<RAW>(oacc[md], va, pbf[g][0], pbf[g][1]);
             }
         }
         __syncwarp();
     }
 
+    // ---- per-head sums from C2 (row ROW1: sum p; rows g: sum p vlo_g), and
+    // o_d = acc_d / f_d + sum p vlo_g
+    const float l0 = __shfl_sync(0xffffffffu, c2[0], ROW1 * 4 + qc);
+    const float l1 = __shfl_sync(0xffffffffu, c2[1], ROW1 * 4 + qc);
+    if constexpr (!RAW) {
+        float sl0[NG], sl1[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+            sl0[g] = __shfl_sync(0xffffffffu, c2[0], g * 4 + qc);
+            sl1[g] = __shfl_sync(0xffffffffu, c2[1], g * 4 + qc);
+        }
+        // rows d = 16md + qr (+8): pair index d/2, factor set by (qr >> 1)
+        const float inv_f = 1.f / pair_factor<BITS>(qr >> 1);
+#pragma unroll
+        for (int md = 0; md < KS; ++md) {
+            const int g = md / 4;
+            oacc[md][0] = oacc[md][0] * inv_f + sl0[g];
+            oacc[md][1] = oacc[md][1] * inv_f + sl1[g];
+            oacc[md][2] = oacc[md][2] * inv_f + sl0[g];
+            oacc[md][3] = oacc[md][3] * inv_f + sl1[g];
+        }
+    }
+
     // ---- merge the 8 warps (fixed order) into the CTA partial
     __syncthreads();
-    float* wo = reinterpret_cast<float*>(vtile);          // [warps][8 heads][D]  (reuses the V tiles)
+    float* wo = reinterpret_cast<float*>(dsm);            // [warps][8 heads][D]  (reuses the rings)
     __shared__ float wm[kDraftWarps][8], wl[kDraftWarps][8];
-    if (qc == 0 && qr < 8) {
-        wm[warp][qr] = m_run;
-        wl[warp][qr] = l_run;
+    if (qr == 0) {
+        wm[warp][2 * qc] = m0;
+        wm[warp][2 * qc + 1] = m1;
+        wl[warp][2 * qc] = l0;
+        wl[warp][2 * qc + 1] = l1;
     }
 #pragma unroll
     for (int md = 0; md < KS; ++md) {
@@ -410,27 +577,32 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
         wo[((size_t)warp * 8 + 2 * qc + 1) * D + d0 + 8] = oacc[md][3];
     }
     __syncthreads();
-    if (threadIdx.x < 8) {
-        const int g = threadIdx.x;
+    __shared__ float wf[kDraftWarps][8];       // exp2(m_warp - m_cta) per (warp, head)
+    if (threadIdx.x < 8 * kDraftWarps) {
+        const int g = threadIdx.x & 7, w = threadIdx.x >> 3;
         float M = -INFINITY;
-        for (int w = 0; w < kDraftWarps; ++w) M = fmaxf(M, wm[w][g]);
-        float L = 0.f;
-        for (int w = 0; w < kDraftWarps; ++w)
-            if (wm[w][g] != -INFINITY) L += wl[w][g] * expf(wm[w][g] - M);
-        cta_m[g] = M;
-        cta_l[g] = L;
+        for (int ww = 0; ww < kDraftWarps; ++ww) M = fmaxf(M, wm[ww][g]);
+        const float f = wm[w][g] == -INFINITY ? 0.f : exp2f(wm[w][g] - M);
+        wf[w][g] = f;
+        if (w == 0) cta_m[g] = M;
     }
     __syncthreads();
+    if (threadIdx.x < 8) {
+        const int g = threadIdx.x;
+        float L = 0.f;
+        for (int w = 0; w < kDraftWarps; ++w) L += wl[w][g] * wf[w][g];
+        cta_l[g] = L;
+    }
     for (int i = threadIdx.x; i < 8 * D; i += blockDim.x) {
         const int g = i / D;
-        const float M = cta_m[g];
         float acc = 0.f;
-        for (int w = 0; w < kDraftWarps; ++w)
-            if (wm[w][g] != -INFINITY) acc += wo[((size_t)w * 8 + g) * D + (i % D)] * expf(wm[w][g] - M);
+#pragma unroll
+        for (int w = 0; w < kDraftWarps; ++w) acc += wo[((size_t)w * 8 + g) * D + (i % D)] * wf[w][g];
         cta_o[i] = acc;
     }
     cluster.sync();
     // ---- cluster merge through distributed shared memory (rank order)
+    __shared__ float rf[8][8];                 // exp2(m_rank - m) / l per (rank, head)
     if (threadIdx.x < 8) {
         const int g = threadIdx.x;
         float M = -INFINITY;
@@ -438,10 +610,14 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
         float L = 0.f;
         for (int r = 0; r < da.cs; ++r) {
             const float mr = cluster.map_shared_rank(cta_m, r)[g];
-            if (mr != -INFINITY) L += cluster.map_shared_rank(cta_l, r)[g] * expf(mr - M);
+            const float f = mr == -INFINITY ? 0.f : exp2f(mr - M);
+            rf[r][g] = f;
+            L += cluster.map_shared_rank(cta_l, r)[g] * f;
         }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        for (int r = 0; r < da.cs; ++r) rf[r][g] *= inv;
         glob_m[g] = M;
-        glob_l[g] = L;
+        glob_l[g] = inv;                       // holds 1 / l from here on
     }
     __syncthreads();
     {
@@ -449,25 +625,34 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
         const int d0 = rank * dper, d1 = min(D, d0 + dper);
         for (int i = threadIdx.x; i < G * (d1 - d0); i += blockDim.x) {
             const int g = i / (d1 - d0), d = d0 + i % (d1 - d0);
-            const float M = glob_m[g];
+            float v[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) v[r] = r < da.cs ? cluster.map_shared_rank(cta_o, r)[g * D + d] : 0.f;
             float acc = 0.f;
-            for (int r = 0; r < da.cs; ++r) {
-                const float mr = cluster.map_shared_rank(cta_m, r)[g];
-                if (mr != -INFINITY) acc += cluster.map_shared_rank(cta_o, r)[g * D + d] * expf(mr - M);
-            }
-            const float o = glob_l[g] > 0.f ? acc / glob_l[g] : 0.f;
-            store_from_f32(a.out, a.out_dtype, ((size_t)b * HQ + h * G + g) * D + d, o);
+#pragma unroll
+            for (int r = 0; r < 8; ++r) acc += r < da.cs ? v[r] * rf[r][g] : 0.f;
+            store_from_f32(a.out, a.out_dtype, ((size_t)b * HQ + h * G + g) * D + d, acc);
         }
     }
     // ---- exact attention mass of this CTA's slots for head h (group sum)
+    const int32_t* cpos = src.cpos + bl * src.cap;
     float* mass_h = a.mass + (bl * a.n_kv + h) * (size_t)src.cap;
-    for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
-        float mv = 0.f;
-        for (int g = 0; g < G; ++g) {
-            const float sc = sbuf[(size_t)g * da.chunk_cap + (s - s0)];
-            if (sc != -INFINITY && glob_l[g] > 0.f) mv += expf(sc - glob_m[g]) / glob_l[g];
+    for (int s = s0 + 4 * threadIdx.x; s < s1; s += 4 * blockDim.x) {
+        float4 mv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s - s0 + 3 < cc) {
+            for (int g = 0; g < G; ++g) {
+                const float4 r = *reinterpret_cast<const float4*>(sbuf + (size_t)g * cc + (s - s0));
+                const float M = glob_m[g], inv = glob_l[g];
+                if (r.x != -INFINITY) mv.x += exp2f(r.x - M) * inv;
+                if (r.y != -INFINITY) mv.y += exp2f(r.y - M) * inv;
+                if (r.z != -INFINITY) mv.z += exp2f(r.z - M) * inv;
+                if (r.w != -INFINITY) mv.w += exp2f(r.w - M) * inv;
+            }
         }
-        mass_h[s] = mv;
+        mass_h[s] = mv.x;
+        if (s + 1 < s1) mass_h[s + 1] = mv.y;
+        if (s + 2 < s1) mass_h[s + 2] = mv.z;
+        if (s + 3 < s1) mass_h[s + 3] = mv.w;
     }
     cluster.sync();   // remote shared memory stays alive until every CTA has read it
     // ---- fold the heads' masses into the scores of this slot range (head order)
@@ -485,25 +670,57 @@ __global__ void __launch_bounds__(kDraftThreads) attn_draft_tc_kernel(DraftArgs 
     __threadfence();
     float* sc_row = a.score + bl * src.cap;
     const float* mass_l = a.mass + bl * a.n_kv * (size_t)src.cap;
-    for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
-        if (__ldcg(cpos + s) < 0) continue;
-        float add = 0.f;
-        for (int hh = 0; hh < a.n_kv; ++hh) add += __ldcg(mass_l + (size_t)hh * src.cap + s);
-        sc_row[s] += add;
+    for (int s = s0 + 4 * threadIdx.x; s < s1; s += 4 * blockDim.x) {
+        float4 add = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int h0 = 0; h0 < a.n_kv; h0 += 4) {
+            float4 mh[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (h0 + u < a.n_kv) mh[u] = __ldcg(reinterpret_cast<const float4*>(mass_l + (size_t)(h0 + u) * src.cap + s));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (h0 + u < a.n_kv) {
+                    add.x += mh[u].x;
+                    add.y += mh[u].y;
+                    add.z += mh[u].z;
+                    add.w += mh[u].w;
+                }
+            }
+        }
+        const int4 cp = __ldcg(reinterpret_cast<const int4*>(cpos + s));
+        if (cp.x >= 0) sc_row[s] += add.x;
+        if (s + 1 < s1 && cp.y >= 0) sc_row[s + 1] += add.y;
+        if (s + 2 < s1 && cp.z >= 0) sc_row[s + 2] += add.z;
+        if (s + 3 < s1 && cp.w >= 0) sc_row[s + 3] += add.w;
     }
 }
 
 uint32_t* device_error_word();
 
+namespace {
+
+struct DraftShape {
+    int stage, vt;
+};
+
 template <int D, int BITS>
-static cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = allow_smem_max(attn_draft_tc_kernel<D, BITS>);
+DraftShape draft_shape() {
+    return {DraftGeo<D, BITS>::STAGE, DraftGeo<D, BITS>::VT};
+}
+
+template <int D, int BITS, int NST>
+cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cudaStream_t st) {
+    static int attr_dev = -1;     // attributes are per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (attr_dev != dev) {
+        e = allow_smem_max(attn_draft_tc_kernel<D, BITS, NST>);
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(attn_draft_tc_kernel<D, BITS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        e = cudaFuncSetAttribute(attn_draft_tc_kernel<D, BITS, NST>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                                 1);
         if (e != cudaSuccess) return e;
-        attr = true;
+        attr_dev = dev;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
@@ -517,8 +734,17 @@ static cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cud
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_draft_tc_kernel<D, BITS>, da);
+    return cudaLaunchKernelEx(&cfg, attn_draft_tc_kernel<D, BITS, NST>, da);
 }
+
+template <int D, int BITS>
+cudaError_t launch_draft_nst(int nst, const DraftArgs& da, dim3 grid, size_t smem, cudaStream_t st) {
+    if (nst >= 4) return launch_draft<D, BITS, 4>(da, grid, smem, st);
+    if (nst == 3) return launch_draft<D, BITS, 3>(da, grid, smem, st);
+    return launch_draft<D, BITS, 2>(da, grid, smem, st);
+}
+
+}  // namespace
 
 int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled,
                  uint32_t* comp_tickets, int raw_dtype);
@@ -531,37 +757,81 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
     const int D = dims.d;
     if ((D != 64 && D != 128) || a.group > 8 || comp_tickets == nullptr) return DKV_OK;
     if (a.src.bits == 16 && raw_dtype != DKV_BF16) return DKV_OK;   // fp32 16-bit entries: generic kernel
+    if (a.src.cap % 16 != 0) return DKV_OK;                         // stages copy whole 16-slot tiles
+    DraftShape shp{};
+    switch (a.src.bits * 1000 + D) {
+        case 2064: shp = draft_shape<64, 2>(); break;
+        case 3064: shp = draft_shape<64, 3>(); break;
+        case 4064: shp = draft_shape<64, 4>(); break;
+        case 8064: shp = draft_shape<64, 8>(); break;
+        case 16064: shp = draft_shape<64, 16>(); break;
+        case 2128: shp = draft_shape<128, 2>(); break;
+        case 3128: shp = draft_shape<128, 3>(); break;
+        case 4128: shp = draft_shape<128, 4>(); break;
+        case 8128: shp = draft_shape<128, 8>(); break;
+        case 16128: shp = draft_shape<128, 16>(); break;
+        default: return DKV_OK;
+    }
+    // Cluster size and ring depth: minimise (waves x slots per CTA), the
+    // per-SM serial work of a bandwidth-bound launch, over cs <= 8 and
+    // NST in {4, 3, 2} (NST = 2 keeps one tile in flight: penalised).
+    constexpr size_t kSmemLimit = 220 * 1024, kSmSmem = 228 * 1024;
+    const int pairs = dims.batch * dims.n_kv;
+    const size_t tail = (size_t)(8 + 8 + 8 * D + 16) * sizeof(float);
+    double best_cost = 0.0;
+    int best_cs = 0, best_nst = 0, best_cap = 0;
+    size_t best_smem = 0, best_region = 0;
+    for (int cs = 1; cs <= 8; ++cs) {
+        const int chunk_cap = ((a.src.cap + cs - 1) / cs + 15) / 16 * 16;
+        for (int nst = 4; nst >= 2; --nst) {
+            const size_t region =
+                std::max((size_t)kDraftWarps * (nst * shp.stage + shp.vt), (size_t)kDraftWarps * 8 * D * 4);
+            const size_t smem = region + (size_t)a.group * chunk_cap * sizeof(float) + tail;
+            if (smem > kSmemLimit) continue;
+            // <= 128 registers a thread (launch bounds): two CTAs per SM when
+            // their shared memory fits
+            const int per_sm = smem + 1024 <= kSmSmem / 2 ? 2 : 1;
+            const int waves = (pairs * cs + 148 * per_sm - 1) / (148 * per_sm);
+            // latency-bound per warp: a CTA alone on its SM is charged 1.5x
+            const double cost = ((double)waves * per_sm * chunk_cap + 64.0 * waves) * (nst == 2 ? 1.15 : 1.0) *
+                                (per_sm == 1 ? 1.5 : 1.0);
+            if (best_cs == 0 || cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best_cs = cs;
+                best_nst = nst;
+                best_cap = chunk_cap;
+                best_smem = smem;
+                best_region = region;
+            }
+        }
+    }
+    if (best_cs == 0) return DKV_OK;       // too many slots per CTA: generic kernel
     DraftArgs da;
     da.a = a;
-    int cs = (2 * 148 + dims.batch * dims.n_kv - 1) / (dims.batch * dims.n_kv);
-    cs = cs < 1 ? 1 : (cs > 8 ? 8 : cs);
-    da.cs = cs;
+    da.cs = best_cs;
+    da.chunk_cap = best_cap;
+    da.region = (int)best_region;
     da.raw_dtype = raw_dtype;
+    da.ch16 = a.src.cb_max % 16 == 0;
     da.tickets = comp_tickets;
     da.err = device_error_word();
     da.a.src.dtype = raw_dtype;
-    // slots per CTA the shared memory must hold (every CTA sizes for the capacity)
-    int per = (a.src.cap + cs - 1) / cs;
-    per = (per + 15) / 16 * 16;
-    da.chunk_cap = per;
-    const size_t fixed = (size_t)kDraftWarps * 16 * D * 2 + (8 + 8 + 8 * D + 16) * sizeof(float);
-    const size_t smem = (size_t)a.group * per * sizeof(float) + std::max(fixed, (size_t)kDraftWarps * 8 * D * 4 + 256);
-    if (smem > 200 * 1024) return DKV_OK;    // too many slots per CTA: generic kernel
-    dim3 grid(cs, dims.n_kv, dims.batch);
+    dim3 grid(best_cs, dims.n_kv, dims.batch);
     cudaError_t e = cudaSuccess;
     {
         ProfScope ps(DKV_PROF_ATTN_COMP, 0.0, st);
+        const int n = best_nst;
         switch (a.src.bits * 1000 + D) {
-            case 2064: e = launch_draft<64, 2>(da, grid, smem, st); break;
-            case 3064: e = launch_draft<64, 3>(da, grid, smem, st); break;
-            case 4064: e = launch_draft<64, 4>(da, grid, smem, st); break;
-            case 8064: e = launch_draft<64, 8>(da, grid, smem, st); break;
-            case 16064: e = launch_draft<64, 16>(da, grid, smem, st); break;
-            case 2128: e = launch_draft<128, 2>(da, grid, smem, st); break;
-            case 3128: e = launch_draft<128, 3>(da, grid, smem, st); break;
-            case 4128: e = launch_draft<128, 4>(da, grid, smem, st); break;
-            case 8128: e = launch_draft<128, 8>(da, grid, smem, st); break;
-            case 16128: e = launch_draft<128, 16>(da, grid, smem, st); break;
+            case 2064: e = launch_draft_nst<64, 2>(n, da, grid, best_smem, st); break;
+            case 3064: e = launch_draft_nst<64, 3>(n, da, grid, best_smem, st); break;
+            case 4064: e = launch_draft_nst<64, 4>(n, da, grid, best_smem, st); break;
+            case 8064: e = launch_draft_nst<64, 8>(n, da, grid, best_smem, st); break;
+            case 16064: e = launch_draft_nst<64, 16>(n, da, grid, best_smem, st); break;
+            case 2128: e = launch_draft_nst<128, 2>(n, da, grid, best_smem, st); break;
+            case 3128: e = launch_draft_nst<128, 3>(n, da, grid, best_smem, st); break;
+            case 4128: e = launch_draft_nst<128, 4>(n, da, grid, best_smem, st); break;
+            case 8128: e = launch_draft_nst<128, 8>(n, da, grid, best_smem, st); break;
+            case 16128: e = launch_draft_nst<128, 16>(n, da, grid, best_smem, st); break;
             default: return DKV_OK;
         }
     }

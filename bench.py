@@ -275,7 +275,7 @@ def run_gpu(args) -> None:
             return [(k, c) for r in allst for k, c in r if k >= 0]
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
-    rounds_needed = args.warmup + args.steps + 4
+    rounds_needed = args.warmup + 2 * args.steps + 13     # timed, profiled, baseline rounds
     vocab = model.vocab_size
     prompts = [[int(x) for x in np.random.default_rng(1 + 1000 * rank + b).integers(0, vocab, ctx)] for b in range(B)]
     max_new = rounds_needed * (G + 1) + 8
@@ -286,11 +286,15 @@ def run_gpu(args) -> None:
     for _ in range(args.warmup):
         sess.round()
 
+    def kept_of(c_, n):
+        return min(n, max(c_.sink + c_.recent, int(round(c_.keep_frac * n))))
+
     def timed_rounds(k, profile):
         toks = 0
         evs = []
         cfgs = {}
         gammas = []
+        dbytes = 0.0       # algorithmic drafter-attention bytes of the rounds (per config used)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -301,6 +305,8 @@ def run_gpu(args) -> None:
         t0 = time.perf_counter()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        if profile:
+            torch.cuda.cudart().cudaProfilerStart()     # ncu --profile-from-start off captures this range
         e0.record()
         for _ in range(k):
             out = sess.round()
@@ -308,7 +314,12 @@ def run_gpu(args) -> None:
             toks += sum(1 + kk for kk, _e in o) if g_r > 0 else len(o)
             cfgs[cfg_r] = cfgs.get(cfg_r, 0) + 1
             gammas.append(g_r)
+            if g_r > 0:
+                dbytes += (g_r * model.n_layers * B * n_kv * kept_of(cfg_r, ctx) * 2
+                           * cfg_r.bytes_per_entry(model.d_head))
         e1.record()
+        if profile:
+            torch.cuda.cudart().cudaProfilerStop()
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
         if world > 1:
@@ -317,9 +328,12 @@ def run_gpu(args) -> None:
         if profile:
             _lib.call("dkv_prof_stop")
         dev_ms = e0.elapsed_time(e1)
-        return toks, dev_ms / 1e3, wall, clocks, cfgs, gammas
+        return toks, dev_ms / 1e3, wall, clocks, cfgs, gammas, dbytes
 
-    toks, dev_s, wall_s, clocks, cfg_counts, gammas = timed_rounds(args.steps, profile=True)
+    # the headline: K rounds with no per-launch events; then the same number
+    # of rounds again with per-launch CUDA events for the kernel roofline
+    toks, dev_s, wall_s, clocks, cfg_counts, gammas, _ = timed_rounds(args.steps, profile=False)
+    _, prof_dev_s, _, _, _, _, d_bytes = timed_rounds(args.steps, profile=True)
     prof = {}
     import ctypes as C
     lib = _lib.load()
@@ -336,7 +350,7 @@ def run_gpu(args) -> None:
     sess.st.comp = None
     base_steps = max(3, min(args.steps, 8))
     sess.round()
-    btoks, bdev_s, bwall_s, _, _, _ = timed_rounds(base_steps, profile=False)
+    btoks, bdev_s, bwall_s, _, _, _, _ = timed_rounds(base_steps, profile=False)
     engine.controller, sess.st.comp = saved_ctrl, saved_comp
 
     # reduce over ranks: max time, summed tokens
@@ -365,12 +379,6 @@ def run_gpu(args) -> None:
     gemm_gbs = g["bytes"] / (g["ms"] / 1e3) / 1e9 if g["ms"] > 0 else 0.0
     kv_elem = 2 if model.dtype == _lib.BF16 else 4
     # attention bandwidth from algorithmic bytes of the launches in the timed region
-    n_draft_steps = sum(gammas)
-    d_bytes = 0.0
-    if n_draft_steps and g["launches"]:
-        c_ = top_cfg
-        kept = min(ctx, max(c_.sink + c_.recent, int(round(c_.keep_frac * ctx))))
-        d_bytes = n_draft_steps * model.n_layers * B * n_kv * kept * 2 * c_.bytes_per_entry(model.d_head)
     v_bytes = rounds * model.n_layers * B * n_kv * ctx * 2 * model.d_head * kv_elem
     a_draft_gbs = d_bytes / (prof["attn_comp"]["ms"] / 1e3) / 1e9 if prof["attn_comp"]["ms"] > 0 else None
     a_full_gbs = v_bytes / (prof["attn_full"]["ms"] / 1e3) / 1e9 if prof["attn_full"]["ms"] > 0 else None

@@ -197,6 +197,7 @@ class CompressedKVCache:
         self.cb_max = d * elem if self._max_bits >= 16 else d * self._max_bits // 8
         if self.dtype == _lib.F32 and self.cb_max < d * 4:
             self.cb_max = max(self.cb_max, 0)
+        cap = -(-cap // 16) * 16          # whole 16-slot tiles (the tensor-core kernel copies tiles)
         self.cap = cap
         dev = "cuda"
         self.k_codes = torch.zeros((B, L, H, cap, self.cb_max), dtype=torch.uint8, device=dev)

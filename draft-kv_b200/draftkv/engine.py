@@ -162,8 +162,8 @@ class DraftKVEngine:
         in chunks, through the full-cache forward."""
         m, B = self.model, st.B
         lens = [len(p) - 1 for p in prompts]
-        CH = 64
         L = max(lens) if lens else 0
+        CH = 256 if L >= 1024 else 64        # long prompts: fewer, larger chunks
         tok = torch.zeros((B, max(L, 1)), dtype=torch.int32)
         for b, p in enumerate(prompts):
             if lens[b] > 0:

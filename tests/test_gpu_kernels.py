@@ -375,3 +375,14 @@ def test_full_attention_matches_torch_and_decode(dtype, G, d):
         L.call("dkv_attn_full", cache.struct(), dims, 0, G, 1, q[t:t + 1].contiguous().data_ptr(), pt.data_ptr(),
                o1.data_ptr(), L.F32, 128, work.data_ptr(), work.numel(), L.stream_ptr())
         assert torch.equal(o1[0], out[t]), t
+
+
+def test_drafter_capacity_is_whole_tiles():
+    """The tensor-core drafter kernel copies 16-slot tiles: every capacity the
+    cache allocates (initial and grown) is a multiple of 16."""
+    from draftkv import CompressedKVCache
+    comp = CompressedKVCache(2, CompressionConfig(4, 0.5), n_kv=2, d_head=64, dtype="bf16", capacity=1000)
+    comp.materialize(2, 64, "bf16") if hasattr(comp, "materialize") else None
+    assert comp.cap % 16 == 0 and comp.cap >= 1000
+    comp._grow(2049)
+    assert comp.cap % 16 == 0 and comp.cap >= 2049

@@ -3,6 +3,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c3|c1|small]
                     [--impl draftkv|reference]
+    python bench.py --kernel draft-attn|verify-attn|gemm [--batch B --ctx C --bits b
+                    --keep f --T t --M m --K k --N n --iters i]     (one kernel alone)
 
 A step is one draft / verify round over every sequence of the batch: gamma
 draft forwards over the compressed cache, one (gamma+1)-token verify forward
@@ -470,6 +472,119 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_kernel(args) -> None:
+    """One hot-path kernel alone on a seeded synthetic case (for roofline and
+    ncu captures), one JSON line.  Inputs exceed L2 (126 MB) and L2 is
+    flushed between timed launches.
+
+      draft-attn   drafter attention (configuration 2 shape by default:
+                   batch 32, ctx 32768, 8 kv x 128, group 4, int4 keep 0.25)
+      verify-attn  full-cache attention for T query tokens per sequence
+      gemm         weight-streaming GEMM, M x K weights, N tokens
+    """
+    import torch
+    from draftkv import _lib, FullKVCache, CompressedKVCache, CompressionConfig
+    import ctypes as C
+    _lib.load()
+    pk = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    iters = args.iters
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b_ = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b_.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b_) * 1e3)
+        return statistics.median(ts)
+
+    B = args.batch or (32 if args.kernel == "draft-attn" else 4)
+    ctx = args.ctx or 32768
+    n_kv, d, G = 8, 128, 4
+    line = {"kernel": args.kernel}
+
+    def full_cache():
+        full = FullKVCache(1, n_kv, d, "bf16", capacity=ctx + 64, batch=B)
+        for b in range(B):
+            full.ensure(b, ctx + 16)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        # K/V ~ N(0, 1) with 1% of the channels (seeded) scaled x8 as outliers
+        ch = torch.randperm(d, generator=torch.Generator().manual_seed(1))[: max(1, d // 100)].to("cuda")
+        for pool in (full.k_pool, full.v_pool):
+            x = torch.randn(pool.shape, generator=g, device="cuda")
+            x[..., ch] *= 8.0
+            pool.copy_(x.to(torch.bfloat16))
+        for b in range(B):
+            full.set_length(b, ctx)
+        return full
+
+    if args.kernel == "draft-attn":
+        full = full_cache()
+        cfg = CompressionConfig(args.bits, args.keep, 4, 512)
+        comp = CompressedKVCache(1, cfg, n_kv=n_kv, d_head=d, dtype="bf16", capacity=int(ctx * args.keep) + 64,
+                                 batch=B, max_bits=args.bits)
+        comp.sync_from(full, 0)
+        kept = int(comp.meta_t[0, 0, 1])
+        del full
+        torch.cuda.empty_cache()
+        dims = comp.dims()
+        work = torch.zeros(int(_lib.load().dkv_attn_work_bytes(dims, G, 1, ctx + 64, 512, comp.cap)),
+                           dtype=torch.uint8, device="cuda")
+        q = torch.randn((B, n_kv * G, d), device="cuda")
+        qpos = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+        out = torch.zeros((B, n_kv * G * d), dtype=torch.bfloat16, device="cuda")
+        by = B * n_kv * kept * 2 * cfg.bytes_per_entry(d)
+        us = timeit(lambda: _lib.call("dkv_attn_comp", comp.struct(), dims, 0, G, q.data_ptr(), qpos.data_ptr(),
+                                      out.data_ptr(), _lib.BF16, work.data_ptr(), work.numel(), _lib.stream_ptr()))
+        line["config"] = {"batch": B, "ctx": ctx, "kept": kept, "bits": args.bits, "keep": args.keep,
+                          "n_kv": n_kv, "d_head": d, "group": G}
+    elif args.kernel == "verify-attn":
+        full = full_cache()
+        T = args.T
+        work = torch.zeros(int(_lib.load().dkv_attn_work_bytes(full.dims(), G, T, ctx + 64, 512, 0)),
+                           dtype=torch.uint8, device="cuda")
+        qv = torch.randn((B * T, n_kv * G, d), device="cuda")
+        p0 = torch.full((B,), ctx - T, dtype=torch.int32, device="cuda")
+        outv = torch.zeros((B * T, n_kv * G * d), dtype=torch.bfloat16, device="cuda")
+        by = B * n_kv * ctx * 2 * d * 2
+        us = timeit(lambda: _lib.call("dkv_attn_full", full.struct(), full.dims(), 0, G, T, qv.data_ptr(),
+                                      p0.data_ptr(), outv.data_ptr(), _lib.BF16, 512, work.data_ptr(), work.numel(),
+                                      _lib.stream_ptr()))
+        line["config"] = {"batch": B, "ctx": ctx, "T": T, "n_kv": n_kv, "d_head": d, "group": G}
+    else:
+        M, K, N = args.M, args.K, args.N
+        g = torch.Generator(device="cuda").manual_seed(0)
+        W = (torch.randn((M, K), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        Wt = torch.empty_like(W)
+        _lib.call("dkv_pack_weight", W.data_ptr(), M, K, Wt.data_ptr(), _lib.stream_ptr())
+        del W
+        X = torch.randn((N, K), generator=g, device="cuda").to(torch.bfloat16)
+        out = torch.zeros((N, M), dtype=torch.float32, device="cuda")
+        work = torch.zeros(int(_lib.load().dkv_gemm_work_bytes(M, N, K, _lib.BF16)), dtype=torch.uint8,
+                           device="cuda")
+        e = _lib.EpilogueS()
+        e.kind = _lib.EPI_STORE
+        e.out_f32 = out.data_ptr()
+        e.ld_out = M
+        e.act_dtype = _lib.BF16
+        by = M * K * 2 + N * K * 2 + N * M * 4
+        us = timeit(lambda: _lib.call("dkv_gemm", X.data_ptr(), _lib.BF16, Wt.data_ptr(), _lib.BF16, M, N, K,
+                                      C.byref(e), work.data_ptr(), work.numel(), _lib.stream_ptr()))
+        line["config"] = {"M": M, "K": K, "N": N}
+    gbs = by / (us * 1e-6) / 1e9
+    line.update({"us": round(us, 2), "algorithmic_bytes": int(by), "achieved_gbs": round(gbs, 1),
+                 "peak_gbs": round(pk["hbm_gbs"], 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+                 "peak_source": pk["source"], "l2": "flushed between launches (256 MB write)"})
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -480,7 +595,19 @@ def main() -> None:
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "gemm"], default=None,
+                    help="time one kernel alone on a synthetic case instead of the decode step")
+    ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--keep", type=float, default=0.25)
+    ap.add_argument("--T", type=int, default=9)
+    ap.add_argument("--M", type=int, default=28672)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--N", type=int, default=4)
+    ap.add_argument("--iters", type=int, default=10)
     args = ap.parse_args()
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

@@ -268,13 +268,8 @@ def run_gpu(args) -> None:
 
     exchange = None
     if world > 1:
-        def exchange(stats):
-            t = torch.tensor([[k, c] for k, c in stats] + [[-1, -1]] * (B - len(stats)), dtype=torch.int32,
-                             device="cuda")
-            out = [torch.empty_like(t) for _ in range(world)]
-            dist.all_gather(out, t)
-            allst = torch.stack(out).cpu().tolist()
-            return [(k, c) for r in allst for k, c in r if k >= 0]
+        from draftkv.dist import allgather_exchange
+        exchange = allgather_exchange(B, device="cuda")
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
     rounds_needed = args.warmup + 2 * args.steps + 13     # timed, profiled, baseline rounds

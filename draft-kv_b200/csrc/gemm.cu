@@ -446,32 +446,21 @@ __global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int M, int K,
 }
 
 // K split S for an (M, K) GEMM.  One CTA per SM is resident (the weight
-// stages fill shared memory), so S is chosen for wave quantization: the
-// smallest S whose CTA count mtiles*S fills whole waves of 148 SMs to >= 90%
-// (at least one full wave), else the best fill up to 4 waves.  S depends on
-// (M, K) only -- never on the token count -- which keeps every token's
-// reduction order fixed.
+// stages fill shared memory), and a launch of decode-sized GEMMs is bound by
+// per-CTA latency as much as by bandwidth, so S fills at most one wave of 148
+// SMs with few, long CTAs: S = floor(128 / row tiles), capped at 4 and at the
+// number of 256-wide k chunks (measured on B200: 4096 x 4096 is fastest at
+// S = 4, 6144 x 4096 at S = 2, 28672 x 4096 and the 128256-row head at S = 1).
+// S depends on (M, K) only -- never on the token count -- which keeps every
+// token's reduction order fixed.
 uint32_t* device_error_word();
 
 int choose_split(int M, int K) {
     const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
-    const int KT = K / 16;
-    const int max_s = KT / kChunkSteps > 0 ? (KT / kChunkSteps < 32 ? KT / kChunkSteps : 32) : 1;
-    constexpr int kSMs = 148;
-    int best = 1;
-    double best_eff = -1.0;
-    for (int S = 1; S <= max_s; ++S) {
-        const int ctas = mtiles * S;
-        const int waves = (ctas + kSMs - 1) / kSMs;
-        if (waves > 4 && best_eff >= 0.0) break;
-        const double eff = ctas < kSMs ? (double)ctas / kSMs : (double)ctas / ((double)waves * kSMs);
-        if (eff >= 0.9) return S;
-        if (eff > best_eff + 1e-9) {
-            best_eff = eff;
-            best = S;
-        }
-    }
-    return best;
+    const int max_s = K / kChunkK > 0 ? K / kChunkK : 1;
+    int S = 128 / mtiles;
+    S = S < 1 ? 1 : (S > 4 ? 4 : S);
+    return S < max_s ? S : max_s;
 }
 
 }  // namespace dkv

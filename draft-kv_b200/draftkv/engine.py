@@ -28,6 +28,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
+from .dist import replicated_select, replicated_update
 from . import _lib
 from .compress import CompressedKVCache
 from .config import CompressionConfig, layer_cfgs
@@ -249,10 +250,12 @@ class DraftKVEngine:
     def session(self, prompts: list, max_new_tokens: int, temperature: float = 0.0,
                 context_key: str | None = None, exchange=None) -> "Session":
         """Prefills `prompts` and returns a Session whose round() runs one
-        draft / verify round.  `exchange`, when given, maps this process's
-        per-sequence [(accepted, ctx)] to the list over every process (the
-        multi-GPU stats all-gather); the controller is updated with that list,
-        so replicated controllers stay identical."""
+        draft / verify round.  `exchange` (see draftkv.dist), when given,
+        maps this process's records to the records of every process; the
+        controller selects on the largest context over all processes and is
+        updated with every process's (accepted, context, gamma), so replicated
+        controllers stay identical.  Every process must call round() the same
+        number of times."""
         return Session(self, [list(p) for p in prompts], max_new_tokens, temperature, context_key, exchange)
 
     # -------------------------------------------------------- device round
@@ -356,10 +359,13 @@ class Session:
         eng, st, m, B = self.eng, self.st, self.m, self.B
         left = [self.max_new - (len(self.toks[b]) - self.plen) for b in range(B)]
         active = [lft > 0 for lft in left]
-        if not any(active):
-            return []
         n = [len(self.toks[b]) for b in range(B)]
-        cfg, gamma = eng.controller.select(max(n), self.key)
+        # every process selects on the same (largest) context: replicated
+        # controllers stay identical
+        cfg, gamma = replicated_select(eng.controller, max(n), self.key, self.exchange)
+        if not any(active):
+            replicated_update(eng.controller, cfg, [], self.key, self.exchange)
+            return []
         gamma = min(gamma, max(min(l for l, a in zip(left, active) if a) - 1, 0), st.G)
         st.active.copy_(torch.tensor([1 if a else 0 for a in active], dtype=torch.int32), non_blocking=True)
         eng._set_counters(st)
@@ -373,8 +379,8 @@ class Session:
                     self.toks[b].append(out[b][1][0])
                     self.res[b].verify_passes += 1
                     self.res[b].rounds.append(RoundLog(cfg, 0, 0, 1, n[b]))
-            if self.exchange is not None:
-                self.exchange([])        # every process takes part in every round's exchange
+            # every process takes part in every round's exchange
+            replicated_update(eng.controller, cfg, [], self.key, self.exchange)
             self.last = (cfg, 0, out)
             return out
         # drafter cache: create, or rebuild only the layers whose config changed
@@ -409,13 +415,10 @@ class Session:
             self.toks[b].extend(emitted)
             st.full.set_length(b, n[b] - 1 + gamma + 1)
             st.full.truncate_seq(b, n[b] + k)        # rollback (engine.py:216)
-            stats.append((k, n[b]))
+            stats.append((k, n[b], gamma))
             self.res[b].draft_steps += gamma
             self.res[b].verify_passes += 1
             self.res[b].rounds.append(RoundLog(cfg, gamma, k, len(emitted), n[b]))
-        if self.exchange is not None:
-            stats = self.exchange(stats)
-        for k, ctx in stats:
-            eng.controller.update(cfg, gamma, k, ctx, self.key)
+        replicated_update(eng.controller, cfg, stats, self.key, self.exchange)
         self.last = (cfg, gamma, out)
         return out

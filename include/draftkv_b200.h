@@ -239,9 +239,8 @@ DKV_API size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype);
  * dkv_gemm minus the work buffer; the split-K scratch is a fixed array of
  * DKV_GEMM_NOALLOC_SCRATCH_BYTES compiled into the library, held on every
  * GPU that loads it until the process exits.  Shapes whose split-K scratch
- * exceeds it (e.g. M = 8192, K = 4096 at 64 tokens; 4096 x 4096, 4096 x 14336
- * and the 128256-row head fit)
- * return DKV_EINVAL with a message.
+ * exceeds it return DKV_EINVAL with a message (e.g. 4096 x 4096 at 320
+ * tokens; every weight of an 8B-class model fits at up to 64 tokens).
  * Allocates nothing.  The first call on a device does that device's set-up;
  * make it outside stream capture.  All calls on a device share the array:
  * calls that overlap on the GPU race. */

@@ -262,9 +262,240 @@ __global__ void __launch_bounds__(kTcThreads) attn_full_tc_kernel(AttnArgs a) {
     split_merge(a, bhr, b, h, R, r0, ms, ls);
 }
 
+// ---------------------------------------------------------------------------
+// Up to 64 query rows (decode, verify): keys are the MMA rows.  S^T = K Q^T
+// with A = 16 keys of K (ldmatrix from the swizzled tile) and B = Q^T (8 query
+// rows as columns); O^T += V^T P^T with A = V^T (ldmatrix.trans) and
+// B = P^T (movmatrix of the S accumulators); the softmax sum comes from one
+// more product with a row of ones.  Warp (kg, rt) takes keys [16kg, 16kg+16)
+// of every 64-key tile and query rows [8rt, 8rt+8); the 4 key groups merge in
+// a fixed order, so a row's arithmetic does not depend on how many rows share
+// the launch: verify rows equal decode rows bit for bit.  Scores are kept in
+// log2 units (log2 e folded into the query scale); partials store the max in
+// natural units for the split merge.
+constexpr int kKqKG = 4;
+constexpr int kKqNST = 3;
+
+template <int D>
+size_t kq_smem(int RT) {
+    const size_t ring = (size_t)kKqNST * 2 * kTcKT * D * 2;
+    const size_t merge = (size_t)RT * kKqKG * 8 * (D + 2) * sizeof(float);
+    return ring > merge ? ring : merge;
+}
+
+DKV_DEV uint32_t movm_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+    return y;
+}
+
+template <int D, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
+    constexpr int DC = D / 8;      // 16-byte chunks per key row
+    constexpr int KS = D / 16;     // k16 steps over d
+    constexpr int PS = D + 2;
+    constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+    extern __shared__ __align__(128) uint8_t tsm[];
+    __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(tsm);      // [NST][K 64xD | V 64xD]
+    __shared__ float ms[kAttnRB], ls[kAttnRB];
+
+    const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int G = a.group, T = a.T;
+    const int R = T * G;
+    const int nthreads = blockDim.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kg = warp % kKqKG, rt = warp / kKqKG;
+    const int qr = lane >> 2, qc = lane & 3;
+    const int mi = lane >> 3, ri = lane & 7;
+    const int qbase = a.qpos0[b];
+    const int n_keys = qbase + T;
+    const int k0 = s * a.split;
+    const int k1 = min(n_keys, k0 + a.split);
+    const size_t bl = (size_t)b * a.n_layers + a.layer;
+    const int HQ = a.n_kv * G;
+    const KeySrc& src = a.src;
+    const __nv_bfloat16* kpool = reinterpret_cast<const __nv_bfloat16*>(src.k_pool);
+    const __nv_bfloat16* vpool = reinterpret_cast<const __nv_bfloat16*>(src.v_pool);
+    const int32_t* ptab = src.page_table + bl * src.max_pages;
+
+    // ---- Q^T fragments: column = query row 8rt + qr (rows >= R are zero)
+    uint32_t qb[KS][2];
+    {
+        const int r = rt * 8 + qr;
+        const float* qv = r < R ? a.q + (((size_t)b * T + r / G) * HQ + h * G + r % G) * D : nullptr;
+        const float sc = a.scale * kLog2e;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int d0 = kk * 16 + 2 * qc;
+            qb[kk][0] = qv ? pack_bf16(qv[d0] * sc, qv[d0 + 1] * sc) : 0u;
+            qb[kk][1] = qv ? pack_bf16(qv[d0 + 8] * sc, qv[d0 + 9] * sc) : 0u;
+        }
+    }
+    // this thread's S columns: rows 8rt + 2qc (0) and 8rt + 2qc + 1 (1)
+    const int r0 = rt * 8 + 2 * qc;
+    const int qp0 = qbase + r0 / G, qp1 = qbase + (r0 + 1) / G;
+
+    float m0 = -INFINITY, m1 = -INFINITY;
+    float c2[4] = {0.f, 0.f, 0.f, 0.f};
+    float oacc[KS][4];                 // O^T: rows d = 16md + qr (+8), cols query rows 2qc, 2qc+1
+#pragma unroll
+    for (int md = 0; md < KS; ++md) oacc[md][0] = oacc[md][1] = oacc[md][2] = oacc[md][3] = 0.f;
+    const uint32_t ones = qr == 0 ? 0x3F803F80u : 0u;     // bf16 ones in row 0 of the sum product
+
+    const int ntiles = k1 > k0 ? (k1 - k0 + kTcKT - 1) / kTcKT : 0;
+    auto load_tile = [&](int slot, int t0) {
+        __nv_bfloat16* kd = ring + (size_t)slot * 2 * kTcKT * D;
+        __nv_bfloat16* vd = kd + kTcKT * D;
+        for (int i = threadIdx.x; i < kTcKT * DC; i += nthreads) {
+            const int key = i / DC, ch = i % DC;
+            const int kp = t0 + key;
+            const bool ok = kp < k1;
+            size_t off = 0;
+            if (ok) {
+                const int page = ptab[kp / src.page_size];
+                off = (((size_t)page * a.n_kv + h) * src.page_size + kp % src.page_size) * D + ch * 8;
+            }
+            cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
+            cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < kKqNST - 1; ++i) {
+        if (i < ntiles) load_tile(i, k0 + i * kTcKT);
+        asm volatile("cp.async.commit_group;\n" ::);
+    }
+    for (int it = 0; it < ntiles; ++it) {
+        const int t0 = k0 + it * kTcKT;
+        if (it + kKqNST - 1 < ntiles) load_tile((it + kKqNST - 1) % kKqNST, t0 + (kKqNST - 1) * kTcKT);
+        asm volatile("cp.async.commit_group;\n" ::);
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(kKqNST - 1));
+        __syncthreads();
+        const __nv_bfloat16* kt = ring + (size_t)(it % kKqNST) * 2 * kTcKT * D;
+        const __nv_bfloat16* vt = kt + kTcKT * D;
+        // ---- S^T: rows keys 16kg + qr (+8), columns query rows
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            uint32_t af[4];
+            ldsm4(af[0], af[1], af[2], af[3], kt + swz<D>(kg * 16 + (mi & 1) * 8 + ri, 2 * kk + (mi >> 1)));
+            mma_bf16_16816(sc, af, qb[kk][0], qb[kk][1]);
+        }
+        // ---- causal / range mask
+        const int kpa = t0 + kg * 16 + qr, kpb = kpa + 8;
+        if (kpa >= k1 || kpa > qp0) sc[0] = -INFINITY;
+        if (kpa >= k1 || kpa > qp1) sc[1] = -INFINITY;
+        if (kpb >= k1 || kpb > qp0) sc[2] = -INFINITY;
+        if (kpb >= k1 || kpb > qp1) sc[3] = -INFINITY;
+        // ---- online softmax (base 2) of the two rows over the 16 keys
+        float t0m = fmaxf(sc[0], sc[2]), t1m = fmaxf(sc[1], sc[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            t0m = fmaxf(t0m, __shfl_xor_sync(0xffffffffu, t0m, off));
+            t1m = fmaxf(t1m, __shfl_xor_sync(0xffffffffu, t1m, off));
+        }
+        {
+            const float n0 = fmaxf(m0, t0m), n1 = fmaxf(m1, t1m);
+            if (!__all_sync(0xffffffffu, n0 == m0 && n1 == m1)) {
+                const float al0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
+                const float al1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+#pragma unroll
+                for (int md = 0; md < KS; ++md) {
+                    oacc[md][0] *= al0;
+                    oacc[md][1] *= al1;
+                    oacc[md][2] *= al0;
+                    oacc[md][3] *= al1;
+                }
+                c2[0] *= al0;
+                c2[1] *= al1;
+                m0 = n0;
+                m1 = n1;
+            }
+        }
+        const float p0 = sc[0] == -INFINITY ? 0.f : exp2f(sc[0] - m0);
+        const float p1 = sc[1] == -INFINITY ? 0.f : exp2f(sc[1] - m1);
+        const float p2 = sc[2] == -INFINITY ? 0.f : exp2f(sc[2] - m0);
+        const float p3 = sc[3] == -INFINITY ? 0.f : exp2f(sc[3] - m1);
+        const uint32_t pb0 = movm_trans(pack_bf16(p0, p1)), pb1 = movm_trans(pack_bf16(p2, p3));
+        {
+            const uint32_t a2[4] = {ones, 0u, ones, 0u};
+            mma_bf16_16816(c2, a2, pb0, pb1);
+        }
+        // ---- O^T += V^T P^T
+#pragma unroll
+        for (int md = 0; md < KS; ++md) {
+            uint32_t va[4];
+            ldsm4t(va[0], va[1], va[2], va[3], vt + swz<D>(kg * 16 + (mi >> 1) * 8 + ri, 2 * md + (mi & 1)));
+            mma_bf16_16816(oacc[md], va, pb0, pb1);
+        }
+        __syncthreads();          // the ring slot is refilled next
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    __syncthreads();
+
+    // ---- merge the 4 key groups of each row (fixed order) into the split partial
+    const float l0 = __shfl_sync(0xffffffffu, c2[0], qc);
+    const float l1 = __shfl_sync(0xffffffffu, c2[1], qc);
+    float* mrg = reinterpret_cast<float*>(tsm);          // [RT][KG][8 rows][D + 2]
+    {
+        float* mine = mrg + ((size_t)(rt * kKqKG + kg) * 8) * PS;
+#pragma unroll
+        for (int md = 0; md < KS; ++md) {
+            const int d0 = 16 * md + qr;
+            mine[(2 * qc) * PS + 2 + d0] = oacc[md][0];
+            mine[(2 * qc + 1) * PS + 2 + d0] = oacc[md][1];
+            mine[(2 * qc) * PS + 2 + d0 + 8] = oacc[md][2];
+            mine[(2 * qc + 1) * PS + 2 + d0 + 8] = oacc[md][3];
+        }
+        if (qr == 0) {
+            mine[(2 * qc) * PS] = m0;
+            mine[(2 * qc) * PS + 1] = l0;
+            mine[(2 * qc + 1) * PS] = m1;
+            mine[(2 * qc + 1) * PS + 1] = l1;
+        }
+    }
+    __syncthreads();
+    const size_t bhr = (size_t)b * a.n_kv + h;
+    float* mypart = a.part + ((bhr * a.n_splits + s) * kAttnRB) * PS;
+    for (int i = threadIdx.x; i < R * (D + 1); i += nthreads) {
+        const int r = i / (D + 1), e = i % (D + 1);      // e == D: the row's (max, sum)
+        const float* g0 = mrg + ((size_t)((r / 8) * kKqKG) * 8 + r % 8) * PS;
+        float M = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < kKqKG; ++q) M = fmaxf(M, g0[(size_t)q * 8 * PS]);
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < kKqKG; ++q) {
+            const float mq = g0[(size_t)q * 8 * PS];
+            if (mq != -INFINITY) acc += g0[(size_t)q * 8 * PS + (e == D ? 1 : 2 + e)] * exp2f(mq - M);
+        }
+        if (e == D) {
+            mypart[(size_t)r * PS] = M == -INFINITY ? -INFINITY : M * kLn2;
+            mypart[(size_t)r * PS + 1] = acc;
+        } else {
+            mypart[(size_t)r * PS + 2 + e] = acc;
+        }
+    }
+    split_merge(a, bhr, b, h, R, 0, ms, ls);
+}
+
 template <int D>
 size_t full_tc_smem() {
     return (size_t)4 * kTcKT * D * 2 + 2 * kAttnRB * sizeof(float);
+}
+
+template <int D, int MAXT>
+cudaError_t launch_kq(const AttnArgs& a, dim3 grid, int threads, cudaStream_t st) {
+    static int attr_dev = -1;     // attributes are per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (attr_dev != dev) {
+        e = allow_smem_max(attn_kq_kernel<D, MAXT>);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    attn_kq_kernel<D, MAXT><<<grid, threads, kq_smem<D>((threads / 32) / kKqKG), st>>>(a);
+    return cudaGetLastError();
 }
 
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
@@ -292,6 +523,18 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
     DKV_REQUIRE(a.part && a.tickets, "attention: work buffer too small (%zu bytes)", work_bytes);
     dim3 grid(a.n_splits, dims.n_kv, dims.batch * a.n_rb);
     ProfScope ps(DKV_PROF_ATTN_FULL, 0.0, st);
+    if (R <= kAttnRB) {
+        const int RT = (R + 7) / 8;
+        const int threads = 32 * kKqKG * RT;
+        cudaError_t e = cudaSuccess;
+        if (dims.d == 128)
+            e = RT <= 4 ? launch_kq<128, 512>(a, grid, threads, st) : launch_kq<128, 1024>(a, grid, threads, st);
+        else
+            e = RT <= 4 ? launch_kq<64, 512>(a, grid, threads, st) : launch_kq<64, 1024>(a, grid, threads, st);
+        DKV_CUDA(e);
+        *handled = true;
+        return DKV_OK;
+    }
     if (dims.d == 128) {
         static bool attr = false;
         if (!attr) {

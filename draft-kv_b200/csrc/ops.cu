@@ -61,6 +61,63 @@ __global__ void norm_kernel(const float* __restrict__ h, int dm, int layernorm, 
     }
 }
 
+// Register-resident variant (dm % 4 == 0, dm <= 256 * 4 * kNormV): the row
+// is read once as float4 into registers, reduced once (twice for LayerNorm,
+// from registers) and written; no second pass over global memory.
+constexpr int kNormV = 8;       // float4s a thread holds (dm <= 8192)
+
+__global__ void __launch_bounds__(256) norm_reg_kernel(const float* __restrict__ h, int dm, int layernorm,
+                                                       const float* __restrict__ w, const float* __restrict__ bias,
+                                                       float eps, void* x, int x_dtype) {
+    __shared__ float red[32];
+    const int n = blockIdx.x;
+    const float4* row = reinterpret_cast<const float4*>(h + (size_t)n * dm);
+    const int n4 = dm >> 2;
+    float4 v[kNormV];
+#pragma unroll
+    for (int k = 0; k < kNormV; ++k) {
+        const int i = threadIdx.x + k * 256;
+        v[k] = i < n4 ? __ldg(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mu = 0.f;
+    if (layernorm) {
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormV; ++k) sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        mu = block_sum(sum, red) / (float)dm;
+    }
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormV; ++k) {
+        if (threadIdx.x + k * 256 < n4) {
+            const float a = v[k].x - mu, b = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
+            sq += (a * a + b * b) + (c * c + d * d);
+        }
+    }
+    const float inv = 1.0f / sqrtf(block_sum(sq, red) / (float)dm + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    const float4* b4 = reinterpret_cast<const float4*>(bias);
+#pragma unroll
+    for (int k = 0; k < kNormV; ++k) {
+        const int i = threadIdx.x + k * 256;
+        if (i >= n4) continue;
+        const float4 g = __ldg(w4 + i);
+        const float4 bb = b4 ? __ldg(b4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float o0 = (v[k].x - mu) * inv * g.x + bb.x, o1 = (v[k].y - mu) * inv * g.y + bb.y;
+        const float o2 = (v[k].z - mu) * inv * g.z + bb.z, o3 = (v[k].w - mu) * inv * g.w + bb.w;
+        const size_t o = (size_t)n * dm + 4 * (size_t)i;
+        if (x_dtype == DKV_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(x) + o) = make_float4(o0, o1, o2, o3);
+        } else {
+            __nv_bfloat162 p0 = __floats2bfloat162_rn(o0, o1), p1 = __floats2bfloat162_rn(o2, o3);
+            uint2 pk;
+            pk.x = *reinterpret_cast<uint32_t*>(&p0);
+            pk.y = *reinterpret_cast<uint32_t*>(&p1);
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(x) + o) = pk;
+        }
+    }
+}
+
 // ------------------------------------------------------------------ sampling
 struct ArgMax {
     float v;
@@ -90,16 +147,47 @@ DKV_DEV ArgMax block_argmax(ArgMax m, ArgMax* red) {
     return red[0];
 }
 
+// Row argmax; 16-byte aligned rows are read as float4, four loads in flight
+// a thread (the result does not depend on the scan order: larger value, then
+// lower index).
 DKV_DEV ArgMax row_argmax(const float* row, int V, ArgMax* red) {
     ArgMax m{-INFINITY, 0x7fffffff};
-    for (int i = threadIdx.x; i < V; i += blockDim.x) m = better(m, ArgMax{row[i], i});
+    int tail = 0;
+    if (((uintptr_t)row & 15u) == 0) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        const int V4 = V >> 2, bd = blockDim.x;
+        int i = threadIdx.x;
+        for (; i + 3 * bd < V4; i += 4 * bd) {
+            float4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) q[u] = __ldg(r4 + i + u * bd);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = 4 * (i + u * bd);
+                m = better(m, ArgMax{q[u].x, e});
+                m = better(m, ArgMax{q[u].y, e + 1});
+                m = better(m, ArgMax{q[u].z, e + 2});
+                m = better(m, ArgMax{q[u].w, e + 3});
+            }
+        }
+        for (; i < V4; i += bd) {
+            const float4 q = __ldg(r4 + i);
+            m = better(m, ArgMax{q.x, 4 * i});
+            m = better(m, ArgMax{q.y, 4 * i + 1});
+            m = better(m, ArgMax{q.z, 4 * i + 2});
+            m = better(m, ArgMax{q.w, 4 * i + 3});
+        }
+        tail = 4 * V4;
+    }
+    for (int i = tail + threadIdx.x; i < V; i += blockDim.x) m = better(m, ArgMax{row[i], i});
     return block_argmax(m, red);
 }
 
 // sum of exp((l - mx) / T) in double, fixed order
 DKV_DEV double row_expsum(const float* row, int V, float mx, double invT, double* redd) {
     double s = 0.0;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) s += exp(((double)row[i] - (double)mx) * invT);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < V; i += blockDim.x) s += exp(((double)__ldg(row + i) - (double)mx) * invT);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     s = warp_sum_d(s);
     __syncthreads();
@@ -364,7 +452,12 @@ extern "C" int dkv_norm(const float* h, int N, int dm, int layernorm, const floa
     DKV_REQUIRE(h && w && x && N >= 0 && dm > 0, "dkv_norm args");
     if (N == 0) return DKV_OK;
     ProfScope ps(DKV_PROF_NORM, (double)N * dm * (4.0 + (x_dtype == DKV_F32 ? 4.0 : 2.0)), (cudaStream_t)stream);
-    norm_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
+    const bool aligned = ((uintptr_t)h % 16 == 0) && ((uintptr_t)w % 16 == 0) && (!b || (uintptr_t)b % 16 == 0) &&
+                         ((uintptr_t)x % 16 == 0);
+    if (dm % 4 == 0 && dm <= 256 * 4 * kNormV && aligned)
+        norm_reg_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
+    else
+        norm_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
     DKV_LAUNCHED();
     return DKV_OK;
 }

@@ -522,6 +522,7 @@ struct AppendArgs {
     const int32_t* n_rows;
     const int32_t* trunc;
     int advance_seen, layer0;
+    int stage_pos;          // the slot positions are staged in shared memory
     uint32_t* err;
     LayerCfgs cfg;
 };
@@ -552,9 +553,33 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
 
     int hwm = c.meta[bl * 4 + 0];
     const int trunc = a.trunc ? a.trunc[b] : -1;
+    // positions of the slot array, staged in shared memory when they fit
+    // (every pass below reads them; writes go to both copies)
+    int32_t* spos = reinterpret_cast<int32_t*>(ap_smem + (size_t)nw * c.d);
+    int32_t* P = a.stage_pos ? spos : pos;
+    if (a.stage_pos) {
+        // int4 copies, four in flight a thread (pos is 64-byte aligned: cap % 16 == 0)
+        const int n4 = (hwm + 3) >> 2, bd = blockDim.x;
+        const int4* g4 = reinterpret_cast<const int4*>(pos);
+        int4* s4 = reinterpret_cast<int4*>(spos);
+        int i = tid;
+        for (; i + 3 * bd < n4; i += 4 * bd) {
+            int4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldcg(g4 + i + u * bd);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) s4[i + u * bd] = v[u];
+        }
+        for (; i < n4; i += bd) s4[i] = __ldcg(g4 + i);
+        __syncthreads();
+    }
+    auto setp = [&](int s, int v) {
+        pos[s] = v;
+        if (a.stage_pos) spos[s] = v;
+    };
     if (trunc >= 0) {
         for (int s = tid; s < hwm; s += blockDim.x)
-            if (pos[s] >= trunc) pos[s] = -1;
+            if (P[s] >= trunc) setp(s, -1);
     }
     const int R = a.n_rows ? a.n_rows[b] : a.src_rows_max;
     const int p0 = a.pos0 ? a.pos0[b] : 0;
@@ -577,7 +602,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     for (int base = 0; base < hwm; base += blockDim.x) {
         if (sh_found >= R) break;
         const int s = base + tid;
-        const bool empty = s < hwm && pos[s] < 0;
+        const bool empty = s < hwm && P[s] < 0;
         const unsigned ball = __ballot_sync(0xffffffffu, empty);
         if (lane == 0) red_i[wid] = __popc(ball);
         __syncthreads();
@@ -628,7 +653,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
         }
     }
     for (int r = tid; r < R; r += blockDim.x) {
-        pos[slot_list[r]] = p0 + r;
+        setp(slot_list[r], p0 + r);
         score[slot_list[r]] = 0.f;
     }
     __syncthreads();
@@ -642,7 +667,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
         __syncthreads();
         int n_loc = 0, pmax_loc = -1;
         for (int s = tid; s < hwm; s += blockDim.x) {
-            const int p = pos[s];
+            const int p = P[s];
             if (p >= 0) {
                 ++n_loc;
                 pmax_loc = max(pmax_loc, p);
@@ -682,7 +707,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
             }
             // recent-th highest position, from a window below pmax
             for (int s = tid; s < hwm; s += blockDim.x) {
-                const int p = pos[s];
+                const int p = P[s];
                 if (p >= 0 && pmax - p < 1024) atomicOr(&bm_hi[(pmax - p) >> 5], 1u << ((pmax - p) & 31));
             }
             __syncthreads();
@@ -693,7 +718,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
             __syncthreads();
             if (sh_plo == -2) {
                 auto key = [&](int s, unsigned long long* k) {
-                    const int p = pos[s];
+                    const int p = P[s];
                     *k = (unsigned long long)(uint32_t)p;
                     return p >= 0;
                 };
@@ -703,7 +728,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
             }
             if (sh_phi == -2) {
                 auto key = [&](int s, unsigned long long* k) {
-                    const int p = pos[s];
+                    const int p = P[s];
                     *k = (unsigned long long)(uint32_t)p;
                     return p >= 0;
                 };
@@ -714,7 +739,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
             const int plo = sh_plo, phi = sh_phi;
             int fr = 0;
             for (int s = tid; s < hwm; s += blockDim.x) {
-                const int p = pos[s];
+                const int p = P[s];
                 fr += (p > plo && p < phi) ? 1 : 0;
             }
             fr = warp_sum_i(fr);
@@ -729,16 +754,46 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
             __syncthreads();
             const int drop = min(n - budget, sh_free);
             auto free_key = [&](int s, unsigned long long* k) {
-                const int p = pos[s];
+                const int p = P[s];
                 *k = ((unsigned long long)__float_as_uint(score[s]) << 32) | (uint32_t)p;
                 return p > plo && p < phi;
             };
             if (drop > 0 && drop <= 8) {
                 for (int it = 0; it < drop; ++it) {
                     unsigned long long best = ~0ull;
-                    for (int s = tid; s < hwm; s += blockDim.x) {
-                        unsigned long long k;
-                        if (free_key(s, &k) && k < best) best = k;
+                    {
+                        // 4 slots a thread per step (float4 scores), two steps of loads in flight
+                        const int n4 = (hwm + 3) >> 2, bd = blockDim.x;
+                        const float4* sc4 = reinterpret_cast<const float4*>(score);
+                        auto take = [&](int s, float sv) {
+                            if (s < hwm) {
+                                const int p = P[s];
+                                if (p > plo && p < phi) {
+                                    const unsigned long long k =
+                                        ((unsigned long long)__float_as_uint(sv) << 32) | (uint32_t)p;
+                                    if (k < best) best = k;
+                                }
+                            }
+                        };
+                        int i = tid;
+                        for (; i + bd < n4; i += 2 * bd) {
+                            const float4 v0 = __ldcg(sc4 + i), v1 = __ldcg(sc4 + i + bd);
+                            take(4 * i, v0.x);
+                            take(4 * i + 1, v0.y);
+                            take(4 * i + 2, v0.z);
+                            take(4 * i + 3, v0.w);
+                            take(4 * (i + bd), v1.x);
+                            take(4 * (i + bd) + 1, v1.y);
+                            take(4 * (i + bd) + 2, v1.z);
+                            take(4 * (i + bd) + 3, v1.w);
+                        }
+                        for (; i < n4; i += bd) {
+                            const float4 v0 = __ldcg(sc4 + i);
+                            take(4 * i, v0.x);
+                            take(4 * i + 1, v0.y);
+                            take(4 * i + 2, v0.z);
+                            take(4 * i + 3, v0.w);
+                        }
                     }
                     best = warp_min_u64(best);
                     __syncthreads();
@@ -754,9 +809,11 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
                     }
                     __syncthreads();
                     const unsigned long long m = sh_min;
-                    for (int s = tid; s < hwm; s += blockDim.x) {
-                        unsigned long long k;
-                        if (free_key(s, &k) && k == m) pos[s] = -1;
+                    if (m != ~0ull) {
+                        // live positions are unique: the key's low word names the slot
+                        const int pm = (int)(uint32_t)m;
+                        for (int s = tid; s < hwm; s += blockDim.x)
+                            if (P[s] == pm) setp(s, -1);
                     }
                     __syncthreads();
                 }
@@ -765,7 +822,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
                 __syncthreads();
                 for (int s = tid; s < hwm; s += blockDim.x) {
                     unsigned long long k;
-                    if (free_key(s, &k) && k <= thr) pos[s] = -1;
+                    if (free_key(s, &k) && k <= thr) setp(s, -1);
                 }
                 __syncthreads();
             }
@@ -775,7 +832,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     __syncthreads();
     int last = -1, cnt = 0;
     for (int s = tid; s < hwm; s += blockDim.x)
-        if (pos[s] >= 0) {
+        if (P[s] >= 0) {
             last = max(last, s);
             ++cnt;
         }
@@ -1141,7 +1198,23 @@ extern "C" int dkv_comp_append(const dkv_comp_cache* comp, const dkv_full_cache*
     a.layer0 = layer0;
     a.err = device_error_word();
     DKV_TRY(fill_cfgs(comp, nullptr, n_layer_sel, layer0, dims.d, raw_dtype == DKV_F32 ? 4 : 2, &a.cfg));
-    const size_t smem = (kAppendThreads / 32) * dims.d;
+    // quantization scratch, plus the slot positions when they fit
+    static int attr_dev = -1;
+    static size_t smem_cap = 0;
+    int dev = 0;
+    DKV_CUDA(cudaGetDevice(&dev));
+    if (attr_dev != dev) {
+        DKV_CUDA(allow_smem_max(comp_append_kernel));
+        int optin = 0;
+        DKV_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        cudaFuncAttributes fa;
+        DKV_CUDA(cudaFuncGetAttributes(&fa, comp_append_kernel));
+        smem_cap = (size_t)optin - fa.sharedSizeBytes;
+        attr_dev = dev;
+    }
+    size_t smem = (kAppendThreads / 32) * dims.d;
+    a.stage_pos = smem + (size_t)comp->cap * sizeof(int32_t) <= smem_cap;
+    if (a.stage_pos) smem += (size_t)comp->cap * sizeof(int32_t);
     dim3 grid(n_layer_sel, dims.batch);
     ProfScope ps(DKV_PROF_APPEND, 0.0, (cudaStream_t)stream);
     comp_append_kernel<<<grid, kAppendThreads, smem, (cudaStream_t)stream>>>(a);

@@ -84,11 +84,12 @@ def _dev_comp(cfg, n_layers=2, n_kv=2, d=64, cap=64):
     return CompressedKVCache(n_layers, cfg, n_kv=n_kv, d_head=d, dtype=np.float32, capacity=cap)
 
 
-def test_eviction_trace_matches_reference(golden_dir):
+@pytest.mark.parametrize("cap", [64, 60000])   # positions staged in shared memory / read from global memory
+def test_eviction_trace_matches_reference(golden_dir, cap):
     """Replays the reference trace (append + note_attention, truncation) on the
     device cache: kept positions exact after every step, scores to fp32."""
     states = json.loads((golden_dir / "evict_trace.json").read_text())["states"]
-    comp = _dev_comp(CompressionConfig(bits=4, keep_frac=0.5, sink=2, recent=4))
+    comp = _dev_comp(CompressionConfig(bits=4, keep_frac=0.5, sink=2, recent=4), cap=cap)
     rng = np.random.default_rng(7)
     pos = 0
     for step, want in enumerate(states):

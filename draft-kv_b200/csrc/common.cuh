@@ -1,6 +1,8 @@
 // Shared helpers for the draftkv_b200 kernels (sm_100a).
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -67,6 +69,31 @@ inline cudaError_t allow_smem_max(K kernel) {
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
+
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may
+// start while the previous kernel on the stream is still running: it must
+// execute pdl_wait() before it reads anything an earlier kernel wrote or
+// writes anything an earlier kernel reads.  pdl_trigger() lets the next
+// kernel start early (it still waits for this one to complete in its own
+// pdl_wait()).  Both are no-ops for kernels launched the ordinary way.
+DKV_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+DKV_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" :::); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }

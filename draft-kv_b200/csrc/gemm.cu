@@ -271,12 +271,16 @@ __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
         mbar_expect_tx(bar, bytes);
         bulk_g2s(my_st + (size_t)(ch % NST) * kWChunkBytes, wsrc + (size_t)ch * kWChunkBytes, bytes, bar);
     };
+    pdl_trigger();
     if (lane == 0) {
         for (int i = 0; i < NST; ++i) mbar_init(my_bar + i, 1);
         fence_async_shared();
         for (int ch = 0; ch < NST && ch < nchunks; ++ch) issue(ch);
     }
     __syncwarp();
+    // the weights do not depend on earlier kernels; activations, outputs,
+    // split-K partials and tickets do
+    pdl_wait();
 
     // X chunk loader: rows n0..n0+NB-1, k range [k_lo, k_lo + 128)
     auto load_chunk = [&](int buf, int k_lo) {
@@ -583,7 +587,7 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
             DKV_CUDA(allow_smem_max(gemm_bf16_kernel<NTV>));                            \
             attr = true;                                                                \
         }                                                                               \
-        gemm_bf16_kernel<NTV><<<grid, 256, gemm_smem<NTV>(), st>>>(g);                  \
+        DKV_CUDA(launch_pdl(gemm_bf16_kernel<NTV>, grid, dim3(256), gemm_smem<NTV>(), st, g));     \
         break;                                                                          \
     }
     switch (nt) {

@@ -70,6 +70,8 @@ __global__ void __launch_bounds__(256) norm_reg_kernel(const float* __restrict__
                                                        const float* __restrict__ w, const float* __restrict__ bias,
                                                        float eps, void* x, int x_dtype) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
     const int n = blockIdx.x;
     const float4* row = reinterpret_cast<const float4*>(h + (size_t)n * dm);
     const int n4 = dm >> 2;
@@ -455,7 +457,8 @@ extern "C" int dkv_norm(const float* h, int N, int dm, int layernorm, const floa
     const bool aligned = ((uintptr_t)h % 16 == 0) && ((uintptr_t)w % 16 == 0) && (!b || (uintptr_t)b % 16 == 0) &&
                          ((uintptr_t)x % 16 == 0);
     if (dm % 4 == 0 && dm <= 256 * 4 * kNormV && aligned)
-        norm_reg_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
+        DKV_CUDA(launch_pdl(norm_reg_kernel, dim3(N), dim3(256), 0, (cudaStream_t)stream, h, dm, layernorm, w, b,
+                            eps, x, x_dtype));
     else
         norm_kernel<<<N, 256, 0, (cudaStream_t)stream>>>(h, dm, layernorm, w, b, eps, x, x_dtype);
     DKV_LAUNCHED();

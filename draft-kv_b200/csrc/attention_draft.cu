@@ -234,6 +234,8 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     constexpr int SEGW = RAW ? D / 8 : (BITS == 3 ? D / 64 : D * BITS / 128);   // words per quad segment
     constexpr float kLog2e = 1.4426950408889634f;
     const AttnArgs& a = da.a;
+    pdl_trigger();
+    pdl_wait();         // queries and the appended rows come from the previous kernels
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int h = blockIdx.y, b = blockIdx.z;
@@ -727,13 +729,15 @@ cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cudaStream
     cfg.blockDim = dim3(kDraftThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = da.cs;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, attn_draft_tc_kernel<D, BITS, NST>, da);
 }
 

@@ -298,6 +298,8 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
     extern __shared__ __align__(128) uint8_t tsm[];
     __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(tsm);      // [NST][K 64xD | V 64xD]
     __shared__ float ms[kAttnRB], ls[kAttnRB];
+    pdl_trigger();
+    pdl_wait();         // queries and the new cache rows come from the previous kernel
 
     const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int G = a.group, T = a.T;
@@ -494,8 +496,7 @@ cudaError_t launch_kq(const AttnArgs& a, dim3 grid, int threads, cudaStream_t st
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
-    attn_kq_kernel<D, MAXT><<<grid, threads, kq_smem<D>((threads / 32) / kKqKG), st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(attn_kq_kernel<D, MAXT>, grid, dim3(threads), kq_smem<D>((threads / 32) / kKqKG), st, a);
 }
 
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,

@@ -541,6 +541,8 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     __shared__ unsigned long long sh_min;
     __shared__ int red_i[32];
 
+    pdl_trigger();
+    pdl_wait();         // the rows to append come from the previous kernel
     const int li = blockIdx.x, b = blockIdx.y;
     const int L = a.layer0 + li;
     const CompView& c = a.c;
@@ -1217,7 +1219,7 @@ extern "C" int dkv_comp_append(const dkv_comp_cache* comp, const dkv_full_cache*
     if (a.stage_pos) smem += (size_t)comp->cap * sizeof(int32_t);
     dim3 grid(n_layer_sel, dims.batch);
     ProfScope ps(DKV_PROF_APPEND, 0.0, (cudaStream_t)stream);
-    comp_append_kernel<<<grid, kAppendThreads, smem, (cudaStream_t)stream>>>(a);
+    DKV_CUDA(launch_pdl(comp_append_kernel, grid, dim3(kAppendThreads), smem, (cudaStream_t)stream, a));
     DKV_LAUNCHED();
     return DKV_OK;
 }

@@ -141,9 +141,19 @@ def check(status: int, what: str = "") -> None:
         raise DraftKVError(f"{what or 'draftkv call'} failed (status {status}): {msg}")
 
 
+# True between dkv_prof_start and dkv_prof_stop issued through call(): the
+# engine does not replay CUDA graphs then, so every launch is timed.
+prof_active = False
+
+
 def call(name: str, *args) -> None:
+    global prof_active
     lib = load()
     check(getattr(lib, name)(*args), name)
+    if name == "dkv_prof_start":
+        prof_active = True
+    elif name == "dkv_prof_stop":
+        prof_active = False
 
 
 def ptr(t) -> int | None:

@@ -107,6 +107,7 @@ class _Batch:
         self.rs = torch.zeros((3, B), dtype=torch.int32, device=dev)
         self.active = torch.ones((B,), dtype=torch.int32, device=dev)
         self.counters = torch.zeros((gamma_max + 2,), dtype=torch.int64, device=dev)
+        self.pos_draft = torch.zeros((max(gamma_max, 1), B), dtype=torch.int32, device=dev)
         self.ctr_host = torch.zeros((gamma_max + 2,), dtype=torch.int64, pin_memory=True)
         V = m.vocab_size
         self.draft_logits = torch.zeros((max(gamma_max, 1), B, V), dtype=torch.float32, device=dev)
@@ -138,6 +139,7 @@ class DraftKVEngine:
         self.model = model
         self.controller = controller or FixedPolicy(CompressionConfig(4, 0.5), 4)
         self.seed = int(seed)
+
         self.full_cache_factory = full_cache_factory
         self.gamma_max = gamma_max
         self._round = 0
@@ -223,13 +225,17 @@ class DraftKVEngine:
             st.full.ensure(b, n[b] + 1)
         self._set_counters(st)
         work = st.workspace()
-        m.forward_raw(st.full, None, st.vtok.data_ptr(), st.VS, st.base_pos, st.B, 1, st.verify_logits, work,
-                      st.G + 1, st.full.capacity_tokens)
-        _lib.call("dkv_accept", st.verify_logits.data_ptr(), None, st.B, 0, m.vocab_size, float(temperature),
-                  self.seed, st.counters[st.G + 1:].data_ptr(), st.vtok.data_ptr(), st.VS, st.base_pos.data_ptr(),
-                  st.accepted.data_ptr(), st.next.data_ptr(), st.rs[0].data_ptr(), st.rs[1].data_ptr(),
-                  st.rs[2].data_ptr(), st.active.data_ptr(), st.accept_work.data_ptr(), st.accept_work.numel(),
-                  _lib.stream_ptr())
+
+        def body():
+            m.forward_raw(st.full, None, st.vtok.data_ptr(), st.VS, st.base_pos, st.B, 1, st.verify_logits, work,
+                          st.G + 1, st.full.capacity_tokens)
+            _lib.call("dkv_accept", st.verify_logits.data_ptr(), None, st.B, 0, m.vocab_size, float(temperature),
+                      self.seed, st.counters[st.G + 1:].data_ptr(), st.vtok.data_ptr(), st.VS,
+                      st.base_pos.data_ptr(), st.accepted.data_ptr(), st.next.data_ptr(), st.rs[0].data_ptr(),
+                      st.rs[1].data_ptr(), st.rs[2].data_ptr(), st.active.data_ptr(), st.accept_work.data_ptr(),
+                      st.accept_work.numel(), _lib.stream_ptr())
+
+        body()
         for b in range(st.B):
             st.full.set_length(b, n[b] + 1)
 
@@ -297,7 +303,8 @@ class DraftKVEngine:
         work = st.workspace()
         V = m.vocab_size
         for i in range(gamma):
-            pos_i = st.base_pos + i
+            pos_i = st.pos_draft[i]
+            torch.add(st.base_pos, i, out=pos_i)
             m.forward_raw(None, st.comp, st.vtok.data_ptr() + 4 * i, st.VS, pos_i, st.B, 1, st.draft_logits[i], work,
                           st.G + 1, st.full.capacity_tokens)
             _lib.call("dkv_sample", st.draft_logits[i].data_ptr(), st.B, V, float(temperature), self.seed,

@@ -44,6 +44,9 @@ class DeviceDecoder:
         self.device = device
         self.split_keys = split_keys
         self.api_chunk = api_chunk
+        self.use_graphs = True          # replay repeated forwards as CUDA graphs (forward_raw)
+        self._graphs: dict = {}
+        self._graph_seen: set = set()
         if dtype is None:
             dtype = config.get("dtype", "f32")
         self.dtype = dtype_code(dtype)
@@ -152,11 +155,44 @@ class DeviceDecoder:
     # ------------------------------------------------------------ forward
     def forward_raw(self, full, comp, tokens_ptr: int, tok_stride: int, pos0: "torch.Tensor", batch: int, T: int,
                     logits: "torch.Tensor", work: "torch.Tensor", max_T: int, max_ctx: int) -> None:
-        """One native forward for `batch` sequences x T tokens (device pointers)."""
+        """One native forward for `batch` sequences x T tokens (device pointers).
+
+        With `use_graphs` a forward whose arguments (every address, size and
+        the drafter's per-layer configs) have been seen before is replayed as a
+        CUDA graph: the second call with given arguments captures it, later
+        calls replay it.  The token, position and cache contents are read at
+        replay time; only the launch parameters are frozen."""
         step = _lib.StepS(batch, T, tokens_ptr, tok_stride, pos0.data_ptr(), logits.data_ptr(), work.data_ptr(),
                           work.numel(), max_ctx, max_T)
-        _lib.call("dkv_forward", C.byref(self._s), None if full is None else C.byref(full.struct()),
-                  None if comp is None else C.byref(comp.struct()), C.byref(step), _lib.stream_ptr())
+        fs = None if full is None else full.struct()        # (syncs a changed page table first)
+        cs = None if comp is None else comp.struct()
+
+        def run():
+            _lib.call("dkv_forward", C.byref(self._s), None if fs is None else C.byref(fs),
+                      None if cs is None else C.byref(cs), C.byref(step), _lib.stream_ptr())
+
+        if not self.use_graphs or _lib.prof_active:
+            run()
+            return
+        key = (tuple(getattr(step, f) for f, _ in step._fields_),
+               None if fs is None else tuple(getattr(fs, f) for f, _ in fs._fields_),
+               None if cs is None else (tuple(getattr(cs, f) for f, _ in cs._fields_[:12]), tuple(comp.cfgs)),
+               _lib.stream_ptr())
+        g = self._graphs.get(key)
+        if g is not None:
+            g.replay()
+            return
+        if key not in self._graph_seen:       # first call: eager (sets kernel attributes)
+            self._graph_seen.add(key)
+            run()
+            return
+        if len(self._graphs) >= 512:          # stale addresses after reallocations
+            self._graphs.clear()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run()
+        self._graphs[key] = g
+        g.replay()
 
     def forward(self, tokens, cache, start_pos: int):
         """Run `tokens` at positions [start_pos, start_pos + T) against `cache`

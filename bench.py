@@ -53,6 +53,10 @@ CONFIGS = {
     "c3": dict(preset="smollm2-135m", ctx=2048, batch=16, temperature=1.0, gamma_max=8,
                arms=[(8, 1.0), (4, 0.5), (4, 0.25), (2, 0.25)],
                workload="smollm2-135m-shape bf16, prompt 2048, 16 seq/GPU, T=1.0, 4-arm Thompson"),
+    "c5": dict(preset="llama3-8b", ctx=262144, batch=1, temperature=0.0, gamma_max=8, arms=[(4, 0.25)],
+               offload=True,
+               workload="llama3-8b-shape bf16, ctx 262144, 1 seq/GPU, greedy; full KV in pinned host memory "
+                        "(streamed over the host link by verify), int4 keep0.25 drafter in HBM"),
     "c1": dict(preset="distilgpt2", ctx=128, batch=1, temperature=0.0, gamma_max=4, fixed=(4, 1.0, 4),
                workload="distilgpt2-shape fp32, prompt 128, 1 seq, greedy, 4b/keep1 gamma 4"),
     "small": dict(preset=None, ctx=2048, batch=4, temperature=0.0, gamma_max=8,
@@ -265,8 +269,21 @@ def run_gpu(args) -> None:
     del wts
     torch.cuda.empty_cache()
     n_kv = model.n_kv_heads
+    h2d_bw = None
+    if conf.get("offload"):
+        # the full cache is read over the host link: measure it (pinned -> device)
+        hbuf = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+        dbuf = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+        dbuf.copy_(hbuf, non_blocking=True)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            dbuf.copy_(hbuf, non_blocking=True)
+        torch.cuda.synchronize()
+        h2d_bw = 3 * (1 << 30) / (time.perf_counter() - t0)
+        del hbuf, dbuf
     cm = CostModel(n_layers=model.n_layers, n_kv_heads=n_kv, d_head=model.d_head, weight_bytes=float(model.weight_bytes),
-                   bandwidth=pk["hbm_gbs"] * 1e9, batch=B)
+                   bandwidth=pk["hbm_gbs"] * 1e9, batch=B, **({"full_kv_bandwidth": h2d_bw} if h2d_bw else {}))
     if "fixed" in conf:
         b_, k_, g_ = conf["fixed"]
         ctrl = FixedPolicy(CompressionConfig(b_, k_), g_)
@@ -280,6 +297,7 @@ def run_gpu(args) -> None:
         exchange = allgather_exchange(B, device="cuda")
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
+    engine.offload_full = bool(conf.get("offload"))
     rounds_needed = args.warmup + 2 * args.steps + 13     # timed, profiled, baseline rounds
     vocab = model.vocab_size
     prompts = [[int(x) for x in np.random.default_rng(1 + 1000 * rank + b).integers(0, vocab, ctx)] for b in range(B)]
@@ -420,7 +438,10 @@ def run_gpu(args) -> None:
         "config": {"workload": conf["workload"], "ctx": ctx, "seqs_per_gpu": B, "global_seqs": B * world, "attn_split_keys": split,
                    "temperature": T, "gamma_max": G, "arms": len(getattr(ctrl, "arms", [1])),
                    "parallelism": f"dp{world} (sequences sharded by rank)",
-                   "l2": "inputs > L2 (weights 15 GB + KV 17 GB stream every round)"},
+                   "l2": f"inputs > L2 (weights {model.weight_bytes / 1e9:.1f} GB + full KV "
+                         f"{B * model.n_layers * 2 * n_kv * model.d_head * 2 * ctx / 1e9:.1f} GB stream every round)",
+                   "full_kv": "pinned host memory" if conf.get("offload") else "HBM",
+                   **({"h2d_gbs": round(h2d_bw / 1e9, 1)} if h2d_bw else {})},
         "speedup_vs_full_kv": round(speedup, 4),
         "full_kv_decode_tps": round(base_tps, 3),
         "ceiling": round(ceiling, 4),

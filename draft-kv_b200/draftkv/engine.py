@@ -139,6 +139,9 @@ class DraftKVEngine:
         self.model = model
         self.controller = controller or FixedPolicy(CompressionConfig(4, 0.5), 4)
         self.seed = int(seed)
+        # keep the full cache in pinned host memory after the prefill (the
+        # drafter cache stays in HBM); verify streams it over the host link
+        self.offload_full = False
 
         self.full_cache_factory = full_cache_factory
         self.gamma_max = gamma_max
@@ -195,6 +198,8 @@ class DraftKVEngine:
         if any(len(p) != len(prompts[0]) for p in prompts):
             raise ValueError("generate_batch needs prompts of one length")
         self._prefill(st, prompts)
+        if self.offload_full and hasattr(st.full, "offload_to_host"):
+            st.full.offload_to_host()
         pend = torch.tensor([p[-1] for p in prompts], dtype=torch.int32)
         st.vtok[:, 0] = pend.to(st.vtok.device)
         st.base_pos.fill_(len(prompts[0]) - 1)

@@ -140,6 +140,30 @@ class PagedKVCache:
         self.sync_table()
         return self._struct
 
+    @property
+    def host_resident(self) -> bool:
+        return not self.k_pool.is_cuda
+
+    def offload_to_host(self) -> None:
+        """Moves the K/V pools to pinned host memory (configuration 5: a
+        long context whose full cache is streamed from the host during verify,
+        while the drafter cache stays in HBM).  The kernels read and write the
+        pools in place through their unified addresses over the host link;
+        page tables stay on the device.  Call between rounds."""
+        if self.host_resident:
+            return
+        import torch
+        torch.cuda.current_stream().synchronize()
+        hk = torch.empty(self.k_pool.shape, dtype=self.k_pool.dtype, pin_memory=True)
+        hk.copy_(self.k_pool)
+        self.k_pool = hk
+        hv = torch.empty(self.v_pool.shape, dtype=self.v_pool.dtype, pin_memory=True)
+        hv.copy_(self.v_pool)
+        self.v_pool = hv
+        self._struct.k_pool = self.k_pool.data_ptr()
+        self._struct.v_pool = self.v_pool.data_ptr()
+        torch.cuda.empty_cache()
+
     def dims(self, batch: int | None = None) -> "_lib.DimsS":
         return _lib.DimsS(self.n_layers, self.n_heads, self.d_head, batch or self.batch)
 

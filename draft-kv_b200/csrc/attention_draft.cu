@@ -149,14 +149,15 @@ struct DraftGeo {
     static constexpr int OFF_VSL = OFF_KSL + 16 * NG * 4;
     static constexpr int OFF_POS = OFF_VSL + 16 * NG * 4;
     static constexpr int STAGE = (OFF_POS + 64 + 127) / 128 * 128;
-    static constexpr int VT = RAW ? 0 : 16 * D * 2;     // per-warp f16 V tile
 };
 
 struct DraftArgs {
     AttnArgs a;
     int cs;                 // cluster size (CTAs per (sequence, head))
-    int chunk_cap;          // slots per CTA the shared memory holds
-    int region;             // bytes of the stage rings + V tiles (or the epilogue's warp partials)
+    int chunk_cap;          // slots per CTA the score buffer holds
+    int region;             // bytes of the stage rings (or the epilogue's warp partials)
+    float* gsc;             // raw scores in global memory [batch][n_kv][group][cap], or null:
+                            // in shared memory [group][chunk_cap] after the region
     int raw_dtype;          // dtype of 16-bit entries
     int ch16;               // code rows are 16-byte aligned: 16-byte copies
     uint32_t* tickets;      // comp->tickets [batch][n_layers][64]
@@ -193,35 +194,89 @@ DKV_DEV void smem_k_segment(const uint8_t* kst, int row, int c, uint32_t* w, uin
     }
 }
 
-// Stages this thread's share of V row `row` (elements [c*D/4, (c+1)*D/4)) as
-// the exact f16 values f*c into the warp's swizzled tile.
+// V codes of this thread for one 64-group of a slot row (element-order
+// storage): elements 64 gg + 8 qr .. +7.  4 bits: one word; 8 bits: two
+// words; 2 and 3 bits: the plane-A word of 16 elements (3 bits: and the
+// plane-B unit of the same 16 elements).
 template <int D, int BITS>
-DKV_DEV void stage_v_row(const uint8_t* vst, int row, int c, uint16_t* vt) {
-    using Geo = DraftGeo<D, BITS>;
-    constexpr int EPQ = D / 4;                 // elements of this quad
-    const uint8_t* vv = vst + row * Geo::KB;
-    constexpr int SPAN = BITS == 3 ? EPQ / 4 : EPQ * BITS / 8;      // plane-A bytes for 3 bits
-    uint32_t w[SPAN / 4 > 0 ? SPAN / 4 : 1];
-    uint16_t u[EPQ / 16 > 0 ? EPQ / 16 : 1];
-    {
-        const uint8_t* p = vv + c * SPAN;
+DKV_DEV void load_vwords(const uint8_t* vst, int row, int gg, int qr, uint32_t (&w)[2], uint32_t& u) {
+    const uint8_t* rp = vst + row * DraftGeo<D, BITS>::KB;
+    if (BITS == 4) {
+        w[0] = *reinterpret_cast<const uint32_t*>(rp + 4 * (8 * gg + qr));
+    } else if (BITS == 8) {
+        const uint2 x = *reinterpret_cast<const uint2*>(rp + 8 * (8 * gg + qr));
+        w[0] = x.x;
+        w[1] = x.y;
+    } else {
+        w[0] = *reinterpret_cast<const uint32_t*>(rp + 4 * (4 * gg + (qr >> 1)));
+        if (BITS == 3) u = *reinterpret_cast<const uint16_t*>(rp + D / 4 + 2 * (4 * gg + (qr >> 1)));
+    }
+}
+
+// A operand registers of O^T += X^T P'^T for one 64-group, built from the
+// codes of two slots x (low halves) and y (high halves) with no shared-memory
+// pass: r[2j + h] = (f_j c_x(e), f_j c_y(e)) as exact f16 for element offset
+// e = 2j + h of the thread's 8 elements.  The pair layout keeps even elements
+// in the low half-word and odd ones in the high half-word at the same bit
+// offset, so one byte permutation interleaves the two slots and a masked
+// field (offset 1024 removed by HSUB2) is f_j times the code, f_j =
+// vfactor<BITS>(j).
+template <int BITS>
+DKV_DEV constexpr float vfactor(int j) {
+    return BITS == 4 ? ((j & 1) ? 16.f : 1.f) : BITS == 2 ? (float)(1 << (2 * j)) : 1.f;
+}
+
+template <int BITS>
+DKV_DEV void v_pairs(const uint32_t (&xw)[2], uint32_t xu, const uint32_t (&yw)[2], uint32_t yu, int t,
+                     uint32_t (&r)[8]) {
+    constexpr uint32_t kOne = 0x64006400u;
+    if constexpr (BITS == 4) {
+        const uint32_t ze = __byte_perm(xw[0], yw[0], 0x5410), zo = __byte_perm(xw[0], yw[0], 0x7632);
+        const uint32_t ze8 = ze >> 8, zo8 = zo >> 8;
+        r[0] = (ze & 0x000F000Fu) | kOne;
+        r[1] = (zo & 0x000F000Fu) | kOne;
+        r[2] = (ze & 0x00F000F0u) | kOne;
+        r[3] = (zo & 0x00F000F0u) | kOne;
+        r[4] = (ze8 & 0x000F000Fu) | kOne;
+        r[5] = (zo8 & 0x000F000Fu) | kOne;
+        r[6] = (ze8 & 0x00F000F0u) | kOne;
+        r[7] = (zo8 & 0x00F000F0u) | kOne;
+    } else if constexpr (BITS == 8) {
 #pragma unroll
-        for (int i = 0; i < SPAN / 4; ++i) w[i] = reinterpret_cast<const uint32_t*>(p)[i];
-        if (BITS == 3) {
-            const uint16_t* pb = reinterpret_cast<const uint16_t*>(vv + D / 4) + c * (EPQ / 16);
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t z = __byte_perm(xw[j >> 1], yw[j >> 1], (j & 1) ? 0x7632 : 0x5410);
+            r[2 * j] = __byte_perm(z, 0x64u, 0x4240);
+            r[2 * j + 1] = __byte_perm(z, 0x64u, 0x4341);
+        }
+    } else {
+        uint32_t ze = __byte_perm(xw[0], yw[0], 0x5410), zo = __byte_perm(xw[0], yw[0], 0x7632);
+        if (t) {
+            ze >>= 8;
+            zo >>= 8;
+        }
+        uint32_t zb = 0;
+        if constexpr (BITS == 3) {
+            zb = __byte_perm(xu, yu, 0x5410);
+            if (t) zb >>= 4;
+        }
 #pragma unroll
-            for (int i = 0; i < EPQ / 16; ++i) u[i] = pb[i];
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t z = h ? zo : ze;
+                if constexpr (BITS == 2) {
+                    r[2 * j + h] = (z & (0x00030003u << (2 * j))) | kOne;
+                } else {
+                    const int k = 8 * h + j;      // plane-B bit of this element
+                    const uint32_t hb = (k >= 2 ? (zb >> (k - 2)) : (zb << (2 - k))) & 0x00040004u;
+                    r[2 * j + h] = ((z >> (2 * j)) & 0x00030003u) | hb | kOne;
+                }
+            }
         }
     }
+    const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400u));
 #pragma unroll
-    for (int c8 = 0; c8 < EPQ / 8; ++c8) {
-        const int chunk16 = (c * EPQ) / 8 + c8;
-        const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400u));
-        uint32_t o[4];
-#pragma unroll
-        for (int pi = 0; pi < 4; ++pi) o[pi] = h2_bits(__hsub2(bits_h2(pair_x<BITS>(w, u, c8 * 4 + pi)), k1024));
-        *reinterpret_cast<uint4*>(vt + row * D + ((chunk16 ^ (row & 7)) << 3)) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
+    for (int i = 0; i < 8; ++i) r[i] = h2_bits(__hsub2(bits_h2(r[i]), k1024));
 }
 
 template <int D, int BITS, int NST>
@@ -254,9 +309,19 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
 
     extern __shared__ __align__(128) uint8_t dsm[];
     uint8_t* ring = dsm + (size_t)warp * NST * Geo::STAGE;
-    uint16_t* vt = reinterpret_cast<uint16_t*>(dsm + (size_t)kDraftWarps * NST * Geo::STAGE) + warp * 16 * D;
-    float* sbuf = reinterpret_cast<float*>(dsm + da.region);                // [G][chunk_cap], log2 units
-    float* cta_m = sbuf + (size_t)G * cc;                                   // [8]
+    float* tailp = reinterpret_cast<float*>(dsm + da.region);
+    // raw scores (log2 units) of this CTA's slots: sbuf[g * sst + (s - s0)]
+    float* sbuf;
+    int sst;
+    if (da.gsc) {
+        sbuf = da.gsc + ((size_t)b * a.n_kv + h) * (size_t)G * src.cap + s0;
+        sst = src.cap;
+    } else {
+        sbuf = tailp;
+        sst = cc;
+        tailp += (size_t)G * cc;
+    }
+    float* cta_m = tailp;                                                   // [8]
     float* cta_l = cta_m + 8;                                               // [8]
     float* cta_o = cta_l + 8;                                               // [8][D]
     float* glob_m = cta_o + 8 * D;                                          // [8]
@@ -447,12 +512,12 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         {
             const int h0 = 2 * qc, h1 = 2 * qc + 1;
             if (ina && sa - s0 < cc) {
-                if (h0 < G) sbuf[(size_t)h0 * cc + (sa - s0)] = sc[0];
-                if (h1 < G) sbuf[(size_t)h1 * cc + (sa - s0)] = sc[1];
+                if (h0 < G) sbuf[(size_t)h0 * sst + (sa - s0)] = sc[0];
+                if (h1 < G) sbuf[(size_t)h1 * sst + (sa - s0)] = sc[1];
             }
             if (inb && sb - s0 < cc) {
-                if (h0 < G) sbuf[(size_t)h0 * cc + (sb - s0)] = sc[2];
-                if (h1 < G) sbuf[(size_t)h1 * cc + (sb - s0)] = sc[3];
+                if (h0 < G) sbuf[(size_t)h0 * sst + (sb - s0)] = sc[2];
+                if (h1 < G) sbuf[(size_t)h1 * sst + (sb - s0)] = sc[3];
             }
         }
         // ---- online softmax (base 2) of the two heads over the tile's 16 slots
@@ -502,13 +567,20 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         }
         // ---- P'^T fragments (B of O^T += X^T P'^T)
         uint32_t pbf[NG][2];
-        const uint16_t* vsrc;
         if constexpr (RAW) {
-            // bf16 entries: P in bf16
+            // bf16 entries: P in bf16, V rows by ldmatrix.trans from the stage
             const float2 fa = __half22float2(pa2), fb = __half22float2(pb2);
             pbf[0][0] = movm_t(pk_bf16(fa.x, fa.y));
             pbf[0][1] = movm_t(pk_bf16(fb.x, fb.y));
-            vsrc = reinterpret_cast<const uint16_t*>(st + Geo::OFF_V);
+            const uint16_t* vsrc = reinterpret_cast<const uint16_t*>(st + Geo::OFF_V);
+            const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll
+            for (int md = 0; md < KS; ++md) {
+                uint32_t va[4];
+                const int row = (mi >> 1) * 8 + ri;
+                ldsm4t_(va, vsrc + row * D + (((2 * md + (mi & 1)) ^ (row & 7)) << 3));
+                mma16816<true>(oacc[md], va, pbf[0][0], pbf[0][1]);
+            }
         } else {
             const uint32_t* vsl = reinterpret_cast<const uint32_t*>(st + Geo::OFF_VSL);
 #pragma unroll
@@ -518,20 +590,29 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                 pbf[g][0] = movm_t(h2_bits(__hmul2(pa2, sa2)));
                 pbf[g][1] = movm_t(h2_bits(__hmul2(pb2, sb2)));
             }
-            stage_v_row<D, BITS>(st + Geo::OFF_V, qr, qc, vt);
-            stage_v_row<D, BITS>(st + Geo::OFF_V, qr + 8, qc, vt);
-            __syncwarp();
-            vsrc = vt;
-        }
-        {
-            const int mi = lane >> 3, ri = lane & 7;
+            // tile md = 4 gg + j: rows qr / qr + 8 are elements 64 gg + 8 qr + 2j (+1),
+            // columns the slots 2qc, 2qc+1 (k 0-7) and 2qc+8, 2qc+9 (k 8-15)
+            const uint8_t* vst = st + Geo::OFF_V;
 #pragma unroll
-            for (int md = 0; md < KS; ++md) {
-                uint32_t va[4];
-                const int row = (mi >> 1) * 8 + ri;
-                ldsm4t_(va, vsrc + row * D + (((2 * md + (mi & 1)) ^ (row & 7)) << 3));
-                const int g = RAW ? 0 : md / 4;
-                mma16816<RAW>(oacc[md], va, pbf[g][0], pbf[g][1]);
+            for (int gg = 0; gg < NG; ++gg) {
+                uint32_t ra[8], rb[8];
+                {
+                    uint32_t xw[2] = {0u, 0u}, yw[2] = {0u, 0u}, xu = 0u, yu = 0u;
+                    load_vwords<D, BITS>(vst, 2 * qc, gg, qr, xw, xu);
+                    load_vwords<D, BITS>(vst, 2 * qc + 1, gg, qr, yw, yu);
+                    v_pairs<BITS>(xw, xu, yw, yu, qr & 1, ra);
+                }
+                {
+                    uint32_t xw[2] = {0u, 0u}, yw[2] = {0u, 0u}, xu = 0u, yu = 0u;
+                    load_vwords<D, BITS>(vst, 2 * qc + 8, gg, qr, xw, xu);
+                    load_vwords<D, BITS>(vst, 2 * qc + 9, gg, qr, yw, yu);
+                    v_pairs<BITS>(xw, xu, yw, yu, qr & 1, rb);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t va[4] = {ra[2 * j], ra[2 * j + 1], rb[2 * j], rb[2 * j + 1]};
+                    mma16816<false>(oacc[4 * gg + j], va, pbf[gg][0], pbf[gg][1]);
+                }
             }
         }
         __syncwarp();
@@ -548,11 +629,10 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
             sl0[g] = __shfl_sync(0xffffffffu, c2[0], g * 4 + qc);
             sl1[g] = __shfl_sync(0xffffffffu, c2[1], g * 4 + qc);
         }
-        // rows d = 16md + qr (+8): pair index d/2, factor set by (qr >> 1)
-        const float inv_f = 1.f / pair_factor<BITS>(qr >> 1);
 #pragma unroll
         for (int md = 0; md < KS; ++md) {
             const int g = md / 4;
+            const float inv_f = 1.f / vfactor<BITS>(md % 4);
             oacc[md][0] = oacc[md][0] * inv_f + sl0[g];
             oacc[md][1] = oacc[md][1] * inv_f + sl1[g];
             oacc[md][2] = oacc[md][2] * inv_f + sl0[g];
@@ -572,11 +652,13 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     }
 #pragma unroll
     for (int md = 0; md < KS; ++md) {
-        const int d0 = 16 * md + qr;
+        // element of rows qr / qr + 8 of tile md
+        const int d0 = RAW ? 16 * md + qr : 64 * (md / 4) + 8 * qr + 2 * (md % 4);
+        const int d1 = RAW ? d0 + 8 : d0 + 1;
         wo[((size_t)warp * 8 + 2 * qc) * D + d0] = oacc[md][0];
         wo[((size_t)warp * 8 + 2 * qc + 1) * D + d0] = oacc[md][1];
-        wo[((size_t)warp * 8 + 2 * qc) * D + d0 + 8] = oacc[md][2];
-        wo[((size_t)warp * 8 + 2 * qc + 1) * D + d0 + 8] = oacc[md][3];
+        wo[((size_t)warp * 8 + 2 * qc) * D + d1] = oacc[md][2];
+        wo[((size_t)warp * 8 + 2 * qc + 1) * D + d1] = oacc[md][3];
     }
     __syncthreads();
     __shared__ float wf[kDraftWarps][8];       // exp2(m_warp - m_cta) per (warp, head)
@@ -643,7 +725,9 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         float4 mv = make_float4(0.f, 0.f, 0.f, 0.f);
         if (s - s0 + 3 < cc) {
             for (int g = 0; g < G; ++g) {
-                const float4 r = *reinterpret_cast<const float4*>(sbuf + (size_t)g * cc + (s - s0));
+                const float* rp = sbuf + (size_t)g * sst + (s - s0);
+                const float4 r = da.gsc ? __ldcg(reinterpret_cast<const float4*>(rp))
+                                        : *reinterpret_cast<const float4*>(rp);
                 const float M = glob_m[g], inv = glob_l[g];
                 if (r.x != -INFINITY) mv.x += exp2f(r.x - M) * inv;
                 if (r.y != -INFINITY) mv.y += exp2f(r.y - M) * inv;
@@ -702,12 +786,14 @@ uint32_t* device_error_word();
 namespace {
 
 struct DraftShape {
-    int stage, vt;
+    int stage;
 };
 
 template <int D, int BITS>
 DraftShape draft_shape() {
-    return {DraftGeo<D, BITS>::STAGE, DraftGeo<D, BITS>::VT};
+    DraftShape r;
+    r.stage = DraftGeo<D, BITS>::STAGE;
+    return r;
 }
 
 template <int D, int BITS, int NST>
@@ -755,8 +841,6 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
 
 int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled,
                  uint32_t* comp_tickets, int raw_dtype) {
-    (void)work;
-    (void)work_bytes;
     *handled = false;
     const int D = dims.d;
     if ((D != 64 && D != 128) || a.group > 8 || comp_tickets == nullptr) return DKV_OK;
@@ -776,36 +860,53 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
         case 16128: shp = draft_shape<128, 16>(); break;
         default: return DKV_OK;
     }
-    // Cluster size and ring depth: minimise (waves x slots per CTA), the
-    // per-SM serial work of a bandwidth-bound launch, over cs <= 8 and
-    // NST in {4, 3, 2} (NST = 2 keeps one tile in flight: penalised).
+    // Cluster size, ring depth and score-buffer place.  Modelled time of a
+    // bandwidth-bound launch: waves x (slots streamed by one SM in a wave +
+    // a fixed per-CTA cost: query load, ring fill, merges, mass epilogue),
+    // with a CTA alone on its SM charged 1.5x (it is latency-bound per warp),
+    // a ring of 2 stages (one tile in flight) 1.15x and scores kept in global
+    // memory (an L2 round trip per slot and head) 1.05x.
     constexpr size_t kSmemLimit = 220 * 1024, kSmSmem = 228 * 1024;
+    constexpr double kFixedSlots = 512.0;
     const int pairs = dims.batch * dims.n_kv;
     const size_t tail = (size_t)(8 + 8 + 8 * D + 16) * sizeof(float);
+    // scores in the work arena, past the fixed ticket region that the other
+    // attention kernels keep there (counters that must stay zero between calls)
+    float* gsc = nullptr;
+    if (work) {
+        Arena ar(work, work_bytes);
+        if (ar.take<unsigned>(16384)) gsc = ar.take<float>((size_t)dims.batch * dims.n_kv * a.group * a.src.cap);
+    }
     double best_cost = 0.0;
     int best_cs = 0, best_nst = 0, best_cap = 0;
+    bool best_gl = false;
     size_t best_smem = 0, best_region = 0;
     for (int cs = 1; cs <= 8; ++cs) {
         const int chunk_cap = ((a.src.cap + cs - 1) / cs + 15) / 16 * 16;
+        const int ctas = pairs * cs;
         for (int nst = 4; nst >= 2; --nst) {
-            const size_t region =
-                std::max((size_t)kDraftWarps * (nst * shp.stage + shp.vt), (size_t)kDraftWarps * 8 * D * 4);
-            const size_t smem = region + (size_t)a.group * chunk_cap * sizeof(float) + tail;
-            if (smem > kSmemLimit) continue;
-            // <= 128 registers a thread (launch bounds): two CTAs per SM when
-            // their shared memory fits
-            const int per_sm = smem + 1024 <= kSmSmem / 2 ? 2 : 1;
-            const int waves = (pairs * cs + 148 * per_sm - 1) / (148 * per_sm);
-            // latency-bound per warp: a CTA alone on its SM is charged 1.5x
-            const double cost = ((double)waves * per_sm * chunk_cap + 64.0 * waves) * (nst == 2 ? 1.15 : 1.0) *
-                                (per_sm == 1 ? 1.5 : 1.0);
-            if (best_cs == 0 || cost < best_cost - 1e-9) {
-                best_cost = cost;
-                best_cs = cs;
-                best_nst = nst;
-                best_cap = chunk_cap;
-                best_smem = smem;
-                best_region = region;
+            const size_t region = std::max((size_t)kDraftWarps * nst * shp.stage, (size_t)kDraftWarps * 8 * D * 4);
+            for (int gl = 0; gl < 2; ++gl) {
+                if (gl && !gsc) continue;
+                const size_t smem = region + tail + (gl ? 0 : (size_t)a.group * chunk_cap * sizeof(float));
+                if (smem > kSmemLimit) continue;
+                // <= 128 registers a thread (launch bounds): two CTAs per SM
+                // when their shared memory fits
+                const int per_sm = smem + 1024 <= kSmSmem / 2 ? 2 : 1;
+                const int waves = (ctas + 148 * per_sm - 1) / (148 * per_sm);
+                const int busy = std::min(per_sm, (ctas + 147) / 148);    // CTAs sharing an SM
+                const double cost = (double)waves * ((double)busy * chunk_cap * (nst == 2 ? 1.15 : 1.0) *
+                                                         (busy == 1 ? 1.5 : 1.0) * (gl ? 1.05 : 1.0) +
+                                                     kFixedSlots);
+                if (best_cs == 0 || cost < best_cost - 1e-9) {
+                    best_cost = cost;
+                    best_cs = cs;
+                    best_nst = nst;
+                    best_cap = chunk_cap;
+                    best_gl = gl != 0;
+                    best_smem = smem;
+                    best_region = region;
+                }
             }
         }
     }
@@ -815,6 +916,7 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
     da.cs = best_cs;
     da.chunk_cap = best_cap;
     da.region = (int)best_region;
+    da.gsc = best_gl ? gsc : nullptr;
     da.raw_dtype = raw_dtype;
     da.ch16 = a.src.cb_max % 16 == 0;
     da.tickets = comp_tickets;

@@ -219,6 +219,9 @@ KeySrc full_src(const dkv_full_cache* f) {
     k.v_pool = f->v_pool;
     k.page_table = f->page_table;
     k.page_size = f->page_size;
+    k.page_shift = -1;
+    for (int sh = 0; sh < 31; ++sh)
+        if ((1 << sh) == f->page_size) k.page_shift = sh;
     k.max_pages = f->max_pages;
     k.dtype = f->dtype;
     k.comp = false;

@@ -123,8 +123,8 @@ __global__ void __launch_bounds__(kTcThreads) attn_full_tc_kernel(AttnArgs a) {
             const bool ok = kp < k1;
             size_t off = 0;
             if (ok) {
-                const int page = src.page_table[bl * src.max_pages + kp / src.page_size];
-                off = (((size_t)page * a.n_kv + h) * src.page_size + kp % src.page_size) * D + ch * 8;
+                const int page = __ldg(src.page_table + bl * src.max_pages + (kp >> src.page_shift));
+                off = ((((size_t)page * a.n_kv + h) << src.page_shift) + (kp & (src.page_size - 1))) * D + ch * 8;
             }
             cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
             cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
@@ -345,17 +345,19 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
     const uint32_t ones = qr == 0 ? 0x3F803F80u : 0u;     // bf16 ones in row 0 of the sum product
 
     const int ntiles = k1 > k0 ? (k1 - k0 + kTcKT - 1) / kTcKT : 0;
+    const int psh = src.page_shift, pmask = src.page_size - 1;     // power-of-two pages (host-checked)
     auto load_tile = [&](int slot, int t0) {
         __nv_bfloat16* kd = ring + (size_t)slot * 2 * kTcKT * D;
         __nv_bfloat16* vd = kd + kTcKT * D;
+#pragma unroll 4
         for (int i = threadIdx.x; i < kTcKT * DC; i += nthreads) {
             const int key = i / DC, ch = i % DC;
             const int kp = t0 + key;
             const bool ok = kp < k1;
             size_t off = 0;
             if (ok) {
-                const int page = ptab[kp / src.page_size];
-                off = (((size_t)page * a.n_kv + h) * src.page_size + kp % src.page_size) * D + ch * 8;
+                const int page = __ldg(ptab + (kp >> psh));
+                off = ((((size_t)page * a.n_kv + h) << psh) + (kp & pmask)) * D + ch * 8;
             }
             cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
             cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
@@ -509,6 +511,7 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
                  bool* handled) {
     *handled = false;
     if (a.src.dtype != DKV_BF16 || (dims.d != 64 && dims.d != 128) || a.split % kTcKT != 0) return DKV_OK;
+    if (a.src.page_shift < 0) return DKV_OK;     // pages of any other size: generic kernel
     const int R = a.T * a.group;
     a.n_rb = (R + kAttnRB - 1) / kAttnRB;
     a.n_splits = (max_keys + a.split - 1) / a.split;

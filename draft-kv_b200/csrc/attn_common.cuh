@@ -11,6 +11,7 @@ struct KeySrc {
     const void* v_pool;
     const int32_t* page_table;
     int page_size, max_pages, dtype;
+    int page_shift;          // log2(page_size), or -1 when page_size is not a power of two
     // drafter cache
     const uint8_t* k_codes;
     const uint8_t* v_codes;

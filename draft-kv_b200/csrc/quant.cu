@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     __shared__ uint32_t bm_lo[32], bm_hi[32];
     __shared__ __align__(16) unsigned hist[256];   // also read as 64-bit warp partials
     __shared__ unsigned long long sh_prefix;
-    __shared__ int sh_k, sh_hwm, sh_found, sh_n, sh_pmax, sh_plo, sh_phi, sh_free;
+    __shared__ int sh_k, sh_hwm, sh_n, sh_pmax, sh_plo, sh_phi, sh_free;
     __shared__ unsigned long long sh_min;
     __shared__ int red_i[32];
 
@@ -595,38 +595,46 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     if (a.advance_seen && R > 0 && p0 + R > seen) seen = p0 + R;
     __syncthreads();
 
-    // ---- slots for the R new rows: lowest empty slots first, then extend hwm
-    if (tid == 0) {
-        sh_found = 0;
-        sh_hwm = hwm;
-    }
-    __syncthreads();
-    for (int base = 0; base < hwm; base += blockDim.x) {
-        if (sh_found >= R) break;
-        const int s = base + tid;
-        const bool empty = s < hwm && P[s] < 0;
-        const unsigned ball = __ballot_sync(0xffffffffu, empty);
-        if (lane == 0) red_i[wid] = __popc(ball);
+    // ---- slots for the R new rows: the lowest R empty slots in slot order,
+    // then extend hwm.  Warp w counts the empty slots of its contiguous
+    // segment; after one barrier each warp knows how many precede it and
+    // emits its share in order (rows of 32 slots, ballots, no more barriers).
+    {
+        const int seg = ((hwm + nw - 1) / nw + 31) / 32 * 32;
+        const int w0 = min(hwm, wid * seg), w1 = min(hwm, w0 + seg);
+        int cnt = 0;
+        if (R > 0) {
+            for (int base = w0; base < w1; base += 32) {
+                const int s = base + lane;
+                cnt += __popc(__ballot_sync(0xffffffffu, s < w1 && P[s] < 0));
+            }
+        }
+        if (lane == 0) red_i[wid] = cnt;
         __syncthreads();
-        int before = sh_found;
-        for (int w = 0; w < wid; ++w) before += red_i[w];
-        const int idx = before + __popc(ball & ((1u << lane) - 1u));
-        if (empty && idx < R) slot_list[idx] = s;
-        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < nw; ++w) {
+            before += w < wid ? red_i[w] : 0;
+            total += red_i[w];
+        }
+        if (cnt > 0 && before < R) {
+            int idx = before;
+            for (int base = w0; base < w1 && idx < R; base += 32) {
+                const int s = base + lane;
+                const bool empty = s < w1 && P[s] < 0;
+                const unsigned ball = __ballot_sync(0xffffffffu, empty);
+                const int my = idx + __popc(ball & ((1u << lane) - 1u));
+                if (empty && my < R) slot_list[my] = s;
+                idx += __popc(ball);
+            }
+        }
         if (tid == 0) {
-            int tot = 0;
-            for (int w = 0; w < nw; ++w) tot += red_i[w];
-            sh_found = min(R, sh_found + tot);
+            int f = min(R, total);
+            int h2 = hwm;
+            while (f < R) slot_list[f++] = h2++;
+            sh_hwm = h2;
         }
         __syncthreads();
     }
-    if (tid == 0) {
-        int f = sh_found;
-        int h2 = hwm;
-        while (f < R) slot_list[f++] = h2++;
-        sh_hwm = h2;
-    }
-    __syncthreads();
     hwm = sh_hwm;
     if (hwm > c.cap) {
         if (tid == 0) atomicOr(a.err, 0x20u);

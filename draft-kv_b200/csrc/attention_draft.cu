@@ -18,18 +18,20 @@
 //               group's queries scaled by 1/f (columns = heads, up to 8):
 //               sum_d q_d (1024 + f c_d)/f = sum_d q_d c_d + 1024 sum_d q_d/f,
 //               so s = scale_g (S_g - off_g) + lo_g sum_d q_d;
-//   O^T += X^T P'^T  X = the V pairs (1024 + f c) in a per-warp swizzled f16
-//               tile read by ldmatrix.trans, P'_g = p * vscale_g obtained
-//               from the S accumulators by movmatrix.trans, and at the end
-//               o_d = (acc_d - 1024 sum P'_g) / f_d + sum p * vlo_g.
+//   O^T += X^T P'^T  X = the V codes of slot pairs, byte-permuted straight
+//               from the stage into A registers (1024 + F c) with one factor
+//               F per bit width, P'_g = p * vscale_g obtained from the S
+//               accumulators by movmatrix.trans, and at the end
+//               o_d = (acc_d - 1024 sum P'_g) / F + sum p * vlo_g, with
+//               sum P'_g from one more product with a row of ones.
 // 16-bit entries (raw bf16) take the plain path.  Scores are kept in log2
 // units (log2 e folded into the query scale) so the softmax uses exp2.
-// Raw scores stay in shared memory; after the warps' online-softmax states
-// are merged, the cluster exchanges (max, sum) through distributed shared
-// memory, each CTA writes its share of the output and the exact attention
-// mass of its slots, and the last of the n_kv clusters to finish a slot range
-// folds the per-head masses into the slot scores in head order (atomic
-// ticket, no wait).
+// Raw scores stay in shared memory, or in the work arena when that lets two
+// CTAs share an SM; after the warps' online-softmax states are merged, the
+// cluster exchanges (max, sum) through distributed shared memory, each CTA
+// writes its share of the output and the exact attention mass of its slots,
+// and the last of the n_kv clusters to finish a slot range folds the per-head
+// masses into the slot scores in head order (atomic ticket, no wait).
 #include <cooperative_groups.h>
 
 #include "attn_common.cuh"
@@ -215,15 +217,18 @@ DKV_DEV void load_vwords(const uint8_t* vst, int row, int gg, int qr, uint32_t (
 
 // A operand registers of O^T += X^T P'^T for one 64-group, built from the
 // codes of two slots x (low halves) and y (high halves) with no shared-memory
-// pass: r[2j + h] = (f_j c_x(e), f_j c_y(e)) as exact f16 for element offset
-// e = 2j + h of the thread's 8 elements.  The pair layout keeps even elements
-// in the low half-word and odd ones in the high half-word at the same bit
-// offset, so one byte permutation interleaves the two slots and a masked
-// field (offset 1024 removed by HSUB2) is f_j times the code, f_j =
-// vfactor<BITS>(j).
+// pass: r[2j + h] = (1024 + F c_x(e), 1024 + F c_y(e)) as exact f16 for
+// element offset e = 2j + h of the thread's 8 elements.  The pair layout
+// keeps even elements in the low half-word and odd ones in the high half-word
+// at the same bit offset, so one byte permutation interleaves the two slots;
+// each field is shifted to one fixed position, so every element carries the
+// same power-of-two factor F = vfactor<BITS>() and the offset 1024 is
+// removed once per tile from the accumulators (1024 x sum P', one more
+// product with a row of ones).  F keeps the codes large next to the offset
+// (mean F c >= 56), so the fp32 accumulators lose at most a few bits to it.
 template <int BITS>
-DKV_DEV constexpr float vfactor(int j) {
-    return BITS == 4 ? ((j & 1) ? 16.f : 1.f) : BITS == 2 ? (float)(1 << (2 * j)) : 1.f;
+DKV_DEV constexpr float vfactor() {
+    return BITS == 8 ? 1.f : BITS == 2 ? 64.f : 16.f;
 }
 
 template <int BITS>
@@ -231,52 +236,59 @@ DKV_DEV void v_pairs(const uint32_t (&xw)[2], uint32_t xu, const uint32_t (&yw)[
                      uint32_t (&r)[8]) {
     constexpr uint32_t kOne = 0x64006400u;
     if constexpr (BITS == 4) {
-        const uint32_t ze = __byte_perm(xw[0], yw[0], 0x5410), zo = __byte_perm(xw[0], yw[0], 0x7632);
-        const uint32_t ze8 = ze >> 8, zo8 = zo >> 8;
-        r[0] = (ze & 0x000F000Fu) | kOne;
-        r[1] = (zo & 0x000F000Fu) | kOne;
-        r[2] = (ze & 0x00F000F0u) | kOne;
-        r[3] = (zo & 0x00F000F0u) | kOne;
-        r[4] = (ze8 & 0x000F000Fu) | kOne;
-        r[5] = (zo8 & 0x000F000Fu) | kOne;
-        r[6] = (ze8 & 0x00F000F0u) | kOne;
-        r[7] = (zo8 & 0x00F000F0u) | kOne;
+        // nibble j of each half to bits 4-7 (F = 16)
+        const uint32_t z[2] = {__byte_perm(xw[0], yw[0], 0x5410), __byte_perm(xw[0], yw[0], 0x7632)};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            r[h] = ((z[h] << 4) & 0x00F000F0u) | kOne;
+            r[2 + h] = (z[h] & 0x00F000F0u) | kOne;
+            r[4 + h] = ((z[h] >> 4) & 0x00F000F0u) | kOne;
+            r[6 + h] = ((z[h] >> 8) & 0x00F000F0u) | kOne;
+        }
     } else if constexpr (BITS == 8) {
+        // bytes as f16 mantissas (F = 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const uint32_t z = __byte_perm(xw[j >> 1], yw[j >> 1], (j & 1) ? 0x7632 : 0x5410);
             r[2 * j] = __byte_perm(z, 0x64u, 0x4240);
             r[2 * j + 1] = __byte_perm(z, 0x64u, 0x4341);
         }
+    } else if constexpr (BITS == 2) {
+        // field j (bits 2j of the thread's byte) to bits 6-7 (F = 64)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            uint32_t z = __byte_perm(xw[0], yw[0], h ? 0x7632 : 0x5410);
+            if (t) z >>= 8;
+            r[h] = ((z << 6) & 0x00C000C0u) | kOne;
+            r[2 + h] = ((z << 4) & 0x00C000C0u) | kOne;
+            r[4 + h] = ((z << 2) & 0x00C000C0u) | kOne;
+            r[6 + h] = (z & 0x00C000C0u) | kOne;
+        }
     } else {
-        uint32_t ze = __byte_perm(xw[0], yw[0], 0x5410), zo = __byte_perm(xw[0], yw[0], 0x7632);
-        if (t) {
-            ze >>= 8;
-            zo >>= 8;
-        }
-        uint32_t zb = 0;
-        if constexpr (BITS == 3) {
-            zb = __byte_perm(xu, yu, 0x5410);
-            if (t) zb >>= 4;
-        }
+        // 3 bits: low two bits (plane A, field j at bits 2j) to bits 4-5 and the
+        // high bit (plane B, bit 8h + j) to bit 6 (F = 16)
+        uint32_t zb = __byte_perm(xu, yu, 0x5410);
+        if (t) zb >>= 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int h = 0; h < 2; ++h) {
+            uint32_t z = __byte_perm(xw[0], yw[0], h ? 0x7632 : 0x5410);
+            if (t) z >>= 8;
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const uint32_t z = h ? zo : ze;
-                if constexpr (BITS == 2) {
-                    r[2 * j + h] = (z & (0x00030003u << (2 * j))) | kOne;
-                } else {
-                    const int k = 8 * h + j;      // plane-B bit of this element
-                    const uint32_t hb = (k >= 2 ? (zb >> (k - 2)) : (zb << (2 - k))) & 0x00040004u;
-                    r[2 * j + h] = ((z >> (2 * j)) & 0x00030003u) | hb | kOne;
-                }
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t lo = (j < 2 ? (z << (4 - 2 * j)) : (z >> (2 * j - 4))) & 0x00300030u;
+                const int k = 8 * h + j;
+                const uint32_t hb = (k <= 6 ? (zb << (6 - k)) : (zb >> (k - 6))) & 0x00400040u;
+                r[2 * j + h] = lo | hb | kOne;
             }
         }
     }
-    const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400u));
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = h2_bits(__hsub2(bits_h2(r[i]), k1024));
+}
+
+// 2^x on the SFU (ex2.approx; -inf gives +0)
+DKV_DEV float fast_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
 }
 
 template <int D, int BITS, int NST>
@@ -310,15 +322,13 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     extern __shared__ __align__(128) uint8_t dsm[];
     uint8_t* ring = dsm + (size_t)warp * NST * Geo::STAGE;
     float* tailp = reinterpret_cast<float*>(dsm + da.region);
-    // raw scores (log2 units) of this CTA's slots: sbuf[g * sst + (s - s0)]
+    // raw scores (log2 units) of this CTA's slots, slot-major:
+    // sbuf[(s - s0) * G + g]
     float* sbuf;
-    int sst;
     if (da.gsc) {
-        sbuf = da.gsc + ((size_t)b * a.n_kv + h) * (size_t)G * src.cap + s0;
-        sst = src.cap;
+        sbuf = da.gsc + (((size_t)b * a.n_kv + h) * (size_t)src.cap + s0) * G;
     } else {
         sbuf = tailp;
-        sst = cc;
         tailp += (size_t)G * cc;
     }
     float* cta_m = tailp;                                                   // [8]
@@ -450,8 +460,15 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     // of the slots and row NG = ones, so C2 row g = sum p * vlo_g and row NG =
     // sum p (16-bit entries: row 0 = sum p)
     constexpr int ROW1 = RAW ? 0 : NG;
-    float m0 = -INFINITY, m1 = -INFINITY;
+    // finite start: a fully masked tile leaves the max at -1e30 and every
+    // p = 2^(-inf) = 0 without a special case
+    constexpr float kNoMax = -1e30f;
+    float m0 = kNoMax, m1 = kNoMax;
     float c2[4] = {0.f, 0.f, 0.f, 0.f};
+    // C3 = ones P'^T per 64-group: row 0-7 = sum P'_g (the V offset's weight)
+    float c3[NG][4];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) c3[g][0] = c3[g][1] = c3[g][2] = c3[g][3] = 0.f;
     float oacc[KS][4];                       // O^T: rows d = 16md + qr (+8), cols heads 2qc, 2qc+1
 #pragma unroll
     for (int md = 0; md < KS; ++md) oacc[md][0] = oacc[md][1] = oacc[md][2] = oacc[md][3] = 0.f;
@@ -478,9 +495,13 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                     mma16816<true>(sc, af, qb[kk][0], qb[kk][1]);
                 }
             } else {
+                // accumulators start at -off_g, so they end at S_g - off_g
                 float gs[NG][4];
 #pragma unroll
-                for (int g = 0; g < NG; ++g) gs[g][0] = gs[g][1] = gs[g][2] = gs[g][3] = 0.f;
+                for (int g = 0; g < NG; ++g) {
+                    gs[g][0] = gs[g][2] = -qo0[g];
+                    gs[g][1] = gs[g][3] = -qo1[g];
+                }
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
                     const uint32_t af[4] = {pair_x<BITS>(w0, u0, 2 * kk), pair_x<BITS>(w1, u1, 2 * kk),
@@ -496,8 +517,8 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                         const uint32_t slw = ksl[row * NG + g];
                         const float2 sl2 = __half22float2(bits_h2(slw));
                         const float scl = sl2.x, lo = sl2.y;
-                        sc[2 * hr] += scl * (gs[g][2 * hr] - qo0[g]) + lo * qs0[g];
-                        sc[2 * hr + 1] += scl * (gs[g][2 * hr + 1] - qo1[g]) + lo * qs1[g];
+                        sc[2 * hr] = fmaf(scl, gs[g][2 * hr], fmaf(lo, qs0[g], sc[2 * hr]));
+                        sc[2 * hr + 1] = fmaf(scl, gs[g][2 * hr + 1], fmaf(lo, qs1[g], sc[2 * hr + 1]));
                     }
                 }
             }
@@ -510,14 +531,19 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         if (!(ina && pa >= 0 && pa <= qpos)) sc[0] = sc[1] = -INFINITY;
         if (!(inb && pb >= 0 && pb <= qpos)) sc[2] = sc[3] = -INFINITY;
         {
-            const int h0 = 2 * qc, h1 = 2 * qc + 1;
-            if (ina && sa - s0 < cc) {
-                if (h0 < G) sbuf[(size_t)h0 * sst + (sa - s0)] = sc[0];
-                if (h1 < G) sbuf[(size_t)h1 * sst + (sa - s0)] = sc[1];
-            }
-            if (inb && sb - s0 < cc) {
-                if (h0 < G) sbuf[(size_t)h0 * sst + (sb - s0)] = sc[2];
-                if (h1 < G) sbuf[(size_t)h1 * sst + (sb - s0)] = sc[3];
+            const int h0 = 2 * qc;
+            auto put = [&](int s, float x, float y) {
+                float* p = sbuf + (size_t)(s - s0) * G + h0;
+                if ((G & 1) == 0) {
+                    *reinterpret_cast<float2*>(p) = make_float2(x, y);    // h0 + 1 < G
+                } else {
+                    p[0] = x;
+                    if (h0 + 1 < G) p[1] = y;
+                }
+            };
+            if (h0 < G) {
+                if (ina && sa - s0 < cc) put(sa, sc[0], sc[1]);
+                if (inb && sb - s0 < cc) put(sb, sc[2], sc[3]);
             }
         }
         // ---- online softmax (base 2) of the two heads over the tile's 16 slots
@@ -530,8 +556,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         {
             const float n0 = fmaxf(m0, t0), n1 = fmaxf(m1, t1);
             if (!__all_sync(0xffffffffu, n0 == m0 && n1 == m1)) {
-                const float al0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
-                const float al1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+                const float al0 = fast_ex2(m0 - n0), al1 = fast_ex2(m1 - n1);
 #pragma unroll
                 for (int md = 0; md < KS; ++md) {
                     oacc[md][0] *= al0;
@@ -541,17 +566,18 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                 }
                 c2[0] *= al0;
                 c2[1] *= al1;
+#pragma unroll
+                for (int g = 0; g < NG; ++g) {
+                    c3[g][0] *= al0;
+                    c3[g][1] *= al1;
+                }
                 m0 = n0;
                 m1 = n1;
             }
         }
         // p (f16): slot qr -> pa2 (heads 2qc, 2qc+1), slot qr+8 -> pb2
-        const float e0 = m0 == -INFINITY ? -INFINITY : sc[0] - m0;
-        const float e1 = m1 == -INFINITY ? -INFINITY : sc[1] - m1;
-        const float e2 = m0 == -INFINITY ? -INFINITY : sc[2] - m0;
-        const float e3 = m1 == -INFINITY ? -INFINITY : sc[3] - m1;
-        const __half2 pa2 = __floats2half2_rn(exp2f(e0), exp2f(e1));
-        const __half2 pb2 = __floats2half2_rn(exp2f(e2), exp2f(e3));
+        const __half2 pa2 = __floats2half2_rn(fast_ex2(sc[0] - m0), fast_ex2(sc[1] - m1));
+        const __half2 pb2 = __floats2half2_rn(fast_ex2(sc[2] - m0), fast_ex2(sc[3] - m1));
         // ---- sums: C2 += A2 P^T
         {
             uint32_t a2[4] = {0u, 0u, 0u, 0u};
@@ -613,6 +639,8 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                     const uint32_t va[4] = {ra[2 * j], ra[2 * j + 1], rb[2 * j], rb[2 * j + 1]};
                     mma16816<false>(oacc[4 * gg + j], va, pbf[gg][0], pbf[gg][1]);
                 }
+                const uint32_t ones[4] = {0x3C003C00u, 0u, 0x3C003C00u, 0u};
+                mma16816<false>(c3[gg], ones, pbf[gg][0], pbf[gg][1]);
             }
         }
         __syncwarp();
@@ -629,14 +657,15 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
             sl0[g] = __shfl_sync(0xffffffffu, c2[0], g * 4 + qc);
             sl1[g] = __shfl_sync(0xffffffffu, c2[1], g * 4 + qc);
         }
+        // o = (acc - 1024 sum P'_g) / F + sum p vlo_g
+        constexpr float inv_f = 1.f / vfactor<BITS>();
 #pragma unroll
         for (int md = 0; md < KS; ++md) {
             const int g = md / 4;
-            const float inv_f = 1.f / vfactor<BITS>(md % 4);
-            oacc[md][0] = oacc[md][0] * inv_f + sl0[g];
-            oacc[md][1] = oacc[md][1] * inv_f + sl1[g];
-            oacc[md][2] = oacc[md][2] * inv_f + sl0[g];
-            oacc[md][3] = oacc[md][3] * inv_f + sl1[g];
+            oacc[md][0] = fmaf(-1024.f, c3[g][0], oacc[md][0]) * inv_f + sl0[g];
+            oacc[md][1] = fmaf(-1024.f, c3[g][1], oacc[md][1]) * inv_f + sl1[g];
+            oacc[md][2] = fmaf(-1024.f, c3[g][0], oacc[md][2]) * inv_f + sl0[g];
+            oacc[md][3] = fmaf(-1024.f, c3[g][1], oacc[md][3]) * inv_f + sl1[g];
         }
     }
 
@@ -721,24 +750,32 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     // ---- exact attention mass of this CTA's slots for head h (group sum)
     const int32_t* cpos = src.cpos + bl * src.cap;
     float* mass_h = a.mass + (bl * a.n_kv + h) * (size_t)src.cap;
-    for (int s = s0 + 4 * threadIdx.x; s < s1; s += 4 * blockDim.x) {
-        float4 mv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s - s0 + 3 < cc) {
-            for (int g = 0; g < G; ++g) {
-                const float* rp = sbuf + (size_t)g * sst + (s - s0);
-                const float4 r = da.gsc ? __ldcg(reinterpret_cast<const float4*>(rp))
-                                        : *reinterpret_cast<const float4*>(rp);
-                const float M = glob_m[g], inv = glob_l[g];
-                if (r.x != -INFINITY) mv.x += exp2f(r.x - M) * inv;
-                if (r.y != -INFINITY) mv.y += exp2f(r.y - M) * inv;
-                if (r.z != -INFINITY) mv.z += exp2f(r.z - M) * inv;
-                if (r.w != -INFINITY) mv.w += exp2f(r.w - M) * inv;
+    for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
+        float mv = 0.f;
+        if (s - s0 < cc) {
+            const float* rp = sbuf + (size_t)(s - s0) * G;
+            if ((G & 3) == 0) {
+                for (int g = 0; g < G; g += 4) {
+                    const float4 r = da.gsc ? __ldcg(reinterpret_cast<const float4*>(rp + g))
+                                            : *reinterpret_cast<const float4*>(rp + g);
+                    mv += exp2f(r.x - glob_m[g]) * glob_l[g] + exp2f(r.y - glob_m[g + 1]) * glob_l[g + 1] +
+                          exp2f(r.z - glob_m[g + 2]) * glob_l[g + 2] + exp2f(r.w - glob_m[g + 3]) * glob_l[g + 3];
+                }
+            } else {
+                for (int g = 0; g < G; ++g) mv += exp2f((da.gsc ? __ldcg(rp + g) : rp[g]) - glob_m[g]) * glob_l[g];
             }
         }
-        mass_h[s] = mv.x;
-        if (s + 1 < s1) mass_h[s + 1] = mv.y;
-        if (s + 2 < s1) mass_h[s + 2] = mv.z;
-        if (s + 3 < s1) mass_h[s + 3] = mv.w;
+        mass_h[s] = mv;
+    }
+    if (da.gsc) {
+        // the scores of [s0, s1) are consumed: drop their L2 lines without a
+        // write-back (whole 128-byte lines inside the range only; the lines it
+        // shares with the neighbouring ranges stay)
+        __syncthreads();
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(sbuf);
+        const uintptr_t hi = reinterpret_cast<uintptr_t>(sbuf + (size_t)(s1 - s0) * G);
+        for (uintptr_t q = ((lo + 127) & ~(uintptr_t)127) + 128 * threadIdx.x; q + 128 <= hi; q += 128 * blockDim.x)
+            asm volatile("discard.global.L2 [%0], 128;\n" ::"l"(q) : "memory");
     }
     cluster.sync();   // remote shared memory stays alive until every CTA has read it
     // ---- fold the heads' masses into the scores of this slot range (head order)

@@ -13,14 +13,20 @@
 // chunks and fed through ldmatrix.
 //
 // Determinism / batch invariance: the split of K across CTAs (S) depends
-// only on (M, K), partial sums are reduced in a fixed order by the last CTA
-// of each row tile (atomic ticket, no spin), and a token's column never
-// depends on the other columns, so a token's output is bit-identical whether
-// it is computed with 1 or 64 other tokens.  This is what makes the verify
-// pass reproduce plain decoding exactly.
+// only on (M, K) and the device, partial sums are reduced in a fixed order
+// (bf16: by the CTAs of a thread-block cluster through distributed shared
+// memory; fp32 and the no-alloc entry: by the last CTA of each row tile,
+// atomic ticket, no spin), and a token's column never depends on the other
+// columns, so a token's output is bit-identical whether it is computed with
+// 1 or 64 other tokens.  This is what makes the verify pass reproduce plain
+// decoding exactly.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace dkv {
 
@@ -60,12 +66,14 @@ DKV_DEV float gelu_new(float x) {
 
 DKV_DEV float silu(float x) { return x / (1.0f + expf(-x)); }
 
-// Applies the epilogue to the tile T[n][m] (n < nb valid tokens starting at n0).
-DKV_DEV void run_epilogue(const EpiArgs& e, const float* T, int mtile, int n0, int nb) {
+// Applies the epilogue to the tile T[n][m] (n < nb valid tokens starting at
+// n0), token rows [j0, j1) of it (all rows when j1 < 0).
+DKV_DEV void run_epilogue(const EpiArgs& e, const float* T, int mtile, int n0, int nb, int j0 = 0, int j1 = -1) {
     const int m0 = mtile * kTileM;
-    const int total = kTileM * nb;
+    if (j1 < 0) j1 = nb;
+    const int total = kTileM * (j1 - j0);
     for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
-        const int i = idx % kTileM, j = idx / kTileM;
+        const int i = idx % kTileM, j = j0 + idx / kTileM;
         const int m = m0 + i, n = n0 + j;
         const float acc = T[j * kTileStride + i];
         switch (e.kind) {
@@ -371,6 +379,175 @@ __global__ void __launch_bounds__(256) gemm_bf16_kernel(GemmArgs g) {
     finish_tile(g.epi, tile, NB, mtile, mtiles, nblk, g.S, s, n0, nb, g.ws, g.tickets);
 }
 
+// ---------------------------------------------------------------------------
+// Clustered split-K schedule (every bf16 dkv_gemm call).
+//
+// The S CTAs that split one row tile's K range form a thread-block cluster.
+// After its k range each CTA leaves its partial tile in its own shared
+// memory; every CTA then sums the S partials of its share of the token rows
+// in rank order through distributed shared memory (no global round trip, no
+// ticket: the tail of a split GEMM is one cluster barrier and a few KB of
+// DSMEM reads) and applies the epilogue to those rows.  Clusters are
+// persistent over row tiles (tile = cluster id + i x clusters) and a CTA's
+// weight ring runs on across its tiles, so a GEMM with more row tiles than
+// SMs has no relaunch gap between waves.  S depends on (M, K) only and the
+// partials are summed in a fixed order, so a token's output does not depend
+// on the other tokens of the call.
+template <int NT>   // number of n8 token tiles per CTA (tokens = 8*NT)
+__global__ void __launch_bounds__(256, 1) gemm_bf16_cl_kernel(GemmArgs g) {
+    extern __shared__ __align__(128) uint8_t gsm[];
+    constexpr int NB = 8 * NT;
+    constexpr int NST = gemm_stages<NT>();
+    uint16_t* xs = reinterpret_cast<uint16_t*>(gsm);          // [2][NB][kXStride]
+    uint8_t* wst = gsm + (size_t)2 * NB * kXStride * 2;       // [8 warps][NST][kWChunkBytes]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(wst + (size_t)8 * NST * kWChunkBytes);   // [8][NST]
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = g.S;
+    const int s = S > 1 ? (int)cluster.block_rank() : 0;
+    const int cid = blockIdx.x / S, ncl = gridDim.x / S;
+    const int mtiles = g.M / kTileM;
+    const int nblk = blockIdx.y, n0 = nblk * 64;
+    const int KT = g.K / 16;
+    const int kt0 = (int)((long long)s * KT / S), kt1 = (int)((long long)(s + 1) * KT / S);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint16_t* X = reinterpret_cast<const uint16_t*>(g.x);
+    const int nsteps = kt1 - kt0;
+    const int nchunks = (nsteps + kChunkSteps - 1) / kChunkSteps;
+    const int my_tiles = cid < mtiles ? (mtiles - 1 - cid) / ncl + 1 : 0;
+    const int total = my_tiles * nchunks;        // ring units of this CTA
+    uint8_t* my_st = wst + (size_t)warp * NST * kWChunkBytes;
+    uint64_t* my_bar = bars + warp * NST;
+    // ring unit i: chunk i % nchunks of row tile cid + (i / nchunks) ncl; this
+    // warp's 16 weight rows over the chunk are one contiguous byte range
+    auto issue = [&](int i) {    // lane 0 only
+        const int tile = cid + (i / nchunks) * ncl, ch = i % nchunks;
+        const int steps = min(kChunkSteps, nsteps - ch * kChunkSteps);
+        const uint32_t bytes = (uint32_t)steps * 512u;
+        uint64_t* bar = my_bar + (i % NST);
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(my_st + (size_t)(i % NST) * kWChunkBytes,
+                 reinterpret_cast<const uint8_t*>(g.w) +
+                     ((size_t)(tile * 8 + warp) * KT + kt0 + (size_t)ch * kChunkSteps) * 512,
+                 bytes, bar);
+    };
+    pdl_trigger();
+    if (lane == 0) {
+        for (int i = 0; i < NST; ++i) mbar_init(my_bar + i, 1);
+        fence_async_shared();
+        for (int i = 0; i < NST && i < total; ++i) issue(i);
+    }
+    __syncwarp();
+    // the weights do not depend on earlier kernels; activations and outputs do
+    pdl_wait();
+
+    // X chunk loader: rows n0..n0+NB-1, k range [k_lo, k_lo + 256) within [kt0, kt1)
+    auto load_chunk = [&](int buf, int k_lo) {
+        uint16_t* dst = xs + buf * NB * kXStride;
+        for (int i = threadIdx.x; i < NB * (kChunkK / 8); i += blockDim.x) {
+            const int r = i / (kChunkK / 8), c8 = i % (kChunkK / 8);
+            const int n = n0 + r, k = k_lo + c8 * 8;
+            const bool ok = n < g.N && k < kt1 * 16;
+            cp_async16(dst + r * kXStride + c8 * 8, ok ? (const void*)(X + (size_t)n * g.K + k) : (const void*)X, ok);
+        }
+        cp_async_commit();
+    };
+
+    const int nb = min(NB, g.N - n0);
+    // this CTA's token rows of each tile's epilogue
+    const int j0 = s * nb / S, j1 = (s + 1) * nb / S;
+    bool ok_all = true;
+    int i = 0;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+        const int mtile = cid + ti * ncl;
+        float acc[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        if (nchunks > 0) load_chunk(0, kt0 * 16);
+        for (int ch = 0; ch < nchunks; ++ch, ++i) {
+            if (ch + 1 < nchunks) {
+                load_chunk((ch + 1) & 1, (kt0 + (ch + 1) * kChunkSteps) * 16);
+                cp_async_wait<1>();
+            } else {
+                cp_async_wait<0>();
+            }
+            __syncthreads();
+            const uint16_t* xb = xs + (ch & 1) * NB * kXStride;
+            const bool ready = mbar_wait(my_bar + (i % NST), (uint32_t)((i / NST) & 1), g.err);
+            ok_all = ok_all && ready;
+            const uint4* wa = reinterpret_cast<const uint4*>(my_st + (size_t)(i % NST) * kWChunkBytes) + lane;
+#pragma unroll
+            for (int st = 0; st < kChunkSteps; ++st) {
+                const int kt = kt0 + ch * kChunkSteps + st;
+                if (kt < kt1 && ready) {
+                    const uint4 a = wa[st * 32];
+                    const int kc = st * 16;   // k offset within chunk
+#pragma unroll
+                    for (int j = 0; j + 1 < NT; j += 2) {
+                        uint32_t b0, b1, b2, b3;
+                        const int mi = lane >> 3, r = lane & 7;
+                        const uint16_t* p = xb + (8 * j + (mi >= 2 ? 8 : 0) + r) * kXStride + kc + (mi & 1) * 8;
+                        ldsm_x4(b0, b1, b2, b3, p);
+                        mma_bf16(acc[j], a, b0, b1);
+                        mma_bf16(acc[j + 1], a, b2, b3);
+                    }
+                    if (NT & 1) {
+                        uint32_t b0, b1;
+                        const int mi = (lane >> 3) & 1, r = lane & 7;
+                        const uint16_t* p = xb + (8 * (NT - 1) + r) * kXStride + kc + mi * 8;
+                        ldsm_x2(b0, b1, p);
+                        mma_bf16(acc[NT - 1], a, b0, b1);
+                    }
+                }
+            }
+            // this stage is consumed: refill it with ring unit i + NST
+            __syncwarp();
+            if (lane == 0 && i + NST < total && ok_all) {
+                fence_async_shared();
+                issue(i + NST);
+            }
+            __syncthreads();
+        }
+
+        // ---- partial tile T[n][m] in the X buffers (both consumed)
+        float* tile = reinterpret_cast<float*>(gsm);
+        {
+            const int r = lane >> 2, c = lane & 3;
+            const int mrow = warp * 16 + r;
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const int n = 8 * j + 2 * c;
+                tile[n * kTileStride + mrow] = acc[j][0];
+                tile[(n + 1) * kTileStride + mrow] = acc[j][1];
+                tile[n * kTileStride + mrow + 8] = acc[j][2];
+                tile[(n + 1) * kTileStride + mrow + 8] = acc[j][3];
+            }
+        }
+        if (S > 1) {
+            cluster.sync();
+            // rows [j0, j1): sum of the S partials in rank order, in place (the
+            // other CTAs read only their own rows of this tile)
+            for (int e = threadIdx.x; e < (j1 - j0) * kTileM; e += blockDim.x) {
+                const int o = (j0 + e / kTileM) * kTileStride + e % kTileM;
+                float v = cluster.map_shared_rank(tile, 0)[o];
+                for (int q = 1; q < S; ++q) v += cluster.map_shared_rank(tile, q)[o];
+                tile[o] = v;
+            }
+        }
+        __syncthreads();
+        run_epilogue(g.epi, tile, mtile, n0, nb, j0, j1);
+        // the next tile's X chunks overwrite this tile: every CTA of the
+        // cluster has read its rows of it
+        if (S > 1) cluster.sync();
+        else __syncthreads();
+    }
+    if (!ok_all && lane == 0) {
+        // a copy never completed: wait (bounded) for any still in flight
+        // before the shared memory is released
+        for (int u = max(0, total - NST); u < total; ++u)
+            mbar_wait(my_bar + (u % NST), (uint32_t)((u / NST) & 1), nullptr);
+    }
+}
+
 // fp32 weights [M][K] row-major, CUDA cores.  Warp w owns 16 weight rows of
 // the tile; lanes split k in float4 steps; 4 tokens per CTA; warp sums
 // reduced in a fixed butterfly.
@@ -467,6 +644,90 @@ int choose_split(int M, int K) {
     return S < max_s ? S : max_s;
 }
 
+// Clusters of S CTAs of gemm_bf16_cl_kernel<NT> that can be resident at once
+// on the current device (one CTA per SM; clusters do not span GPCs).
+template <int NT>
+int cl_active(int S) {
+    static int cache[64][9] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || S < 1 || S > 8) return 0;
+    if (cache[dev][S] == 0) {
+        if (allow_smem_max(gemm_bf16_cl_kernel<NT>) != cudaSuccess) return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S * 148);
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = gemm_smem<NT>();
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = S;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_bf16_cl_kernel<NT>, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            return 0;
+        }
+        cache[dev][S] = n;
+    }
+    return cache[dev][S];
+}
+
+// Clusters launched for mtiles row tiles when act fit at once: one per row
+// tile up to two waves, persistent clusters over more row tiles (no gap
+// between the waves of the 1002-tile head).
+int cl_count(int mtiles, int act) { return mtiles <= 2 * act ? mtiles : act; }
+
+// Launches the clustered kernel: ncl clusters of S CTAs per token block,
+// with programmatic dependent launch.
+template <typename Kern>
+cudaError_t launch_cl(Kern kern, int ncl, int S, int nblk, size_t smem, cudaStream_t st, const GemmArgs& g) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ncl * S, nblk);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = S;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = S > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, g);
+}
+
+// K split S of the clustered schedule for an (M, K) GEMM: the S in 1..8 (at
+// most the number of 256-wide k chunks) that minimises the modelled time of
+// one CTA in k steps, rounds x (ceil(KT / S) + 32), where rounds = row tiles
+// per cluster with as many clusters as fit at once and 32 k steps charge the
+// end of a row tile (barriers, partial sums, epilogue: the weight ring runs
+// dry meanwhile; measured on B200, ~2 us), plus 8 k steps per extra partial
+// summed.  The residency used is that of the one-token-tile kernel, so S
+// depends on (M, K) and the device only -- never on the token count.
+int choose_split_cl(int M, int K) {
+    const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
+    const int KT = K / 16;
+    const int max_s = std::max(1, std::min(8, K / kChunkK));
+    int best = 1;
+    double best_cost = 0.0;
+    for (int S = 1; S <= max_s; ++S) {
+        const int act = cl_active<1>(S);
+        if (act <= 0) continue;
+        const int ncl = std::min(mtiles, act);
+        const int rounds = (mtiles + ncl - 1) / ncl;
+        const double cost = (double)rounds * ((KT + S - 1) / S + 32) + 8.0 * (S - 1);
+        if (S == 1 || cost < best_cost - 1e-9) {
+            best = S;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
 }  // namespace dkv
 
 using namespace dkv;
@@ -515,7 +776,8 @@ extern "C" size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype) {
     const int nblk = (N + tok - 1) / tok;
     const size_t tile = (size_t)tok * kTileStride * sizeof(float);
     size_t b = kGemmTickets * sizeof(unsigned);
-    if (S > 1) b += (size_t)nblk * mtiles * S * tile;
+    // bf16: the split-K partials stay in the clusters' shared memory
+    if (w_dtype == DKV_F32 && S > 1) b += (size_t)nblk * mtiles * S * tile;
     return b + 256;
 }
 
@@ -535,8 +797,9 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     DKV_REQUIRE(K % 16 == 0, "dkv_gemm: K (%d) must be a multiple of 16", K);
     if (N == 0) return DKV_OK;
     const int mtiles = M / kTileM;
-    const int S = choose_split(M, K);
-    const int tok = w_dtype == DKV_F32 ? kF32Tok : 64;
+    const bool f32 = w_dtype == DKV_F32;
+    const int S = f32 ? choose_split(M, K) : choose_split_cl(M, K);
+    const int tok = f32 ? kF32Tok : 64;
     const int nblk = (N + tok - 1) / tok;
     DKV_REQUIRE((size_t)nblk * mtiles <= kGemmTickets, "dkv_gemm: too many row tiles x token blocks");
     Arena ar(work, work_bytes);
@@ -549,9 +812,10 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     g.S = S;
     g.tickets = ar.take<unsigned>(kGemmTickets);
     const size_t tile_floats = (size_t)tok * kTileStride;
-    g.ws = S > 1 ? ar.take<float>((size_t)nblk * mtiles * S * tile_floats) : nullptr;
-    DKV_REQUIRE(g.tickets && (S == 1 || g.ws), "dkv_gemm: work buffer too small (%zu bytes, need %zu)", work_bytes,
-                dkv_gemm_work_bytes(M, N, K, w_dtype));
+    // bf16 partials stay in the clusters' shared memory
+    g.ws = f32 && S > 1 ? ar.take<float>((size_t)nblk * mtiles * S * tile_floats) : nullptr;
+    DKV_REQUIRE(g.tickets && (!f32 || S == 1 || g.ws), "dkv_gemm: work buffer too small (%zu bytes, need %zu)",
+                work_bytes, dkv_gemm_work_bytes(M, N, K, w_dtype));
     // columns written: m < min(M, ld_out) (the head is padded to 128 rows;
     // SwiGLU writes d_ff = ld_out columns from 2*d_ff rows)
     int M_real = M;
@@ -579,15 +843,26 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     const int nt = std::min(8, (std::min(N, 64) + 7) / 8);
     g.err = device_error_word();
     // the result tile [NB][kTileStride] reuses the X staging buffers, which
-    // are larger, so the bf16 kernel's shared memory is gemm_smem<NT>()
+    // are larger, so the bf16 kernel's shared memory is gemm_smem<NT>().
+    // Unsplit GEMMs of at most two waves take the plain kernel (one CTA per
+    // row tile, the same arithmetic): measured on B200, the clustered kernel
+    // streams the 224-tile gate/up projection ~10% slower even when launched
+    // without clusters.
 #define DKV_GEMM_CASE(NTV)                                                              \
     case NTV: {                                                                         \
-        static bool attr = false;                                                       \
-        if (!attr) {                                                                    \
-            DKV_CUDA(allow_smem_max(gemm_bf16_kernel<NTV>));                            \
-            attr = true;                                                                \
+        const int act = cl_active<NTV>(S);                                              \
+        DKV_REQUIRE(act > 0, "dkv_gemm: no resident cluster of %d CTAs", S);            \
+        const int ncl = cl_count(mtiles, act);                                          \
+        if (S == 1 && ncl == mtiles) {                                                  \
+            static bool attr = false;                                                   \
+            if (!attr) {                                                                \
+                DKV_CUDA(allow_smem_max(gemm_bf16_kernel<NTV>));                        \
+                attr = true;                                                            \
+            }                                                                           \
+            DKV_CUDA(launch_pdl(gemm_bf16_kernel<NTV>, grid, dim3(256), gemm_smem<NTV>(), st, g)); \
+        } else {                                                                        \
+            DKV_CUDA(launch_cl(gemm_bf16_cl_kernel<NTV>, ncl, S, nblk, gemm_smem<NTV>(), st, g)); \
         }                                                                               \
-        DKV_CUDA(launch_pdl(gemm_bf16_kernel<NTV>, grid, dim3(256), gemm_smem<NTV>(), st, g));     \
         break;                                                                          \
     }
     switch (nt) {

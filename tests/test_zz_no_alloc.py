@@ -87,8 +87,10 @@ def test_no_alloc_f32_gemm_matches_dkv_gemm_twice():
 
 def test_no_alloc_rejects_shapes_beyond_the_fixed_scratch():
     L = _lib()
-    M, K, N = 4096, 4096, 320          # 5 token blocks x 32 row tiles x 4 K splits of partials: ~22 MB
-    need = int(L.load().dkv_gemm_work_bytes(M, N, K, L.BF16))
+    M, K, N = 4096, 4096, 320
+    # the no-alloc entry's split-K partials: 5 token blocks x 32 row tiles x
+    # 4 K splits x a 64 x 132 fp32 tile, ~22 MB
+    need = 5 * 32 * 4 * 64 * 132 * 4
     assert need > LIMIT + (1 << 20)
     x = torch.zeros(16, dtype=torch.bfloat16, device="cuda")     # never read: rejected before launch
     out = torch.zeros(16, dtype=torch.float32, device="cuda")

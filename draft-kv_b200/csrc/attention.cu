@@ -102,10 +102,12 @@ __global__ void __launch_bounds__(kGenThreads) attn_generic_kernel(AttnArgs a) {
                 const int key = kt + j;
                 if (src.comp) {
                     if (src.cpos[bl * src.cap + key] >= 0) {
-                        const size_t vi = (bl * a.n_kv + h) * (size_t)src.cap + key;
+                        const size_t vh = (bl * a.n_kv + h) * (size_t)src.cap;
+                        const size_t vi = vh + key;
                         const int raw = src.cb_max >= d * 4 ? DKV_F32 : DKV_BF16;
-                        kvv = deq_code(src.k_codes + vi * src.cb_max, src.k_sl + vi * (d / 64) * 2, d, src.bits, true, e, raw);
-                        vvv = deq_code(src.v_codes + vi * src.cb_max, src.v_sl + vi * (d / 64) * 2, d, src.bits, false, e, raw);
+                        const size_t co = vh * src.cb_max + (size_t)key * code_row_bytes(d, src.bits, raw);
+                        kvv = deq_code(src.k_codes + co, src.k_sl + vi * (d / 64) * 2, d, src.bits, true, e, raw);
+                        vvv = deq_code(src.v_codes + co, src.v_sl + vi * (d / 64) * 2, d, src.bits, false, e, raw);
                     }
                 } else {
                     const int page = src.page_table[bl * src.max_pages + key / src.page_size];

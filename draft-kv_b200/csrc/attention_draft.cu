@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         if (k < nck && ck < 16 * cpr) {
             const int row = cw == 16 ? ck / (KB / 16 > 0 ? KB / 16 : 1) : ck / (KB / 8);
             const int col = cw == 16 ? ck % (KB / 16 > 0 ? KB / 16 : 1) : ck % (KB / 8);
-            c_go[k] = row * src.cb_max + col * cw;
+            c_go[k] = row * KB + col * cw;
             c_ko[k] = row * KB + col * cw;
             c_vo[k] = Geo::OFF_V + row * KB + (RAW ? ((col ^ (row & 7)) * 16) : col * cw);
         }
@@ -386,8 +386,8 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         if (i < my_n) {
             const int base = (first_tile + warp + i * kDraftWarps) * 16;
             const uint32_t st = ring_s + (uint32_t)((i % NST) * Geo::STAGE);
-            const uint8_t* kt = kbase + (size_t)base * src.cb_max;
-            const uint8_t* vtile = vbase + (size_t)base * src.cb_max;
+            const uint8_t* kt = kbase + (size_t)base * KB;          // rows of KB bytes, dense
+            const uint8_t* vtile = vbase + (size_t)base * KB;
 #pragma unroll
             for (int k = 0; k < MAXC; ++k) {
                 if (c_go[k] >= 0) {

@@ -77,6 +77,14 @@ inline cudaError_t allow_smem_max(K kernel) {
 // writes anything an earlier kernel reads.  pdl_trigger() lets the next
 // kernel start early (it still waits for this one to complete in its own
 // pdl_wait()).  Both are no-ops for kernels launched the ordinary way.
+// Bytes of one drafter-cache vector of d elements at `bits` per element
+// (16: raw entries of raw_dtype).  A layer's vectors are stored densely at
+// this stride inside each (sequence, layer, head) region of cap x cb_max
+// bytes, so a narrow configuration streams contiguous bytes.
+__host__ __device__ inline int code_row_bytes(int d, int bits, int raw_dtype) {
+    return bits >= 16 ? d * (raw_dtype == DKV_F32 ? 4 : 2) : d * bits / 8;
+}
+
 DKV_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 DKV_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" :::); }
 

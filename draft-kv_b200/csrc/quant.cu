@@ -417,6 +417,11 @@ struct CompView {
     DKV_DEV size_t vec(int b, int L, int h, int slot) const {
         return ((bl(b, L) * n_kv + h) * (size_t)cap + slot);
     }
+    // byte offset of a vector's codes: the (b, L, h) region of cap x cb_max
+    // bytes holds rows of kb = code_row_bytes(...) bytes, densely
+    DKV_DEV size_t code_off(int b, int L, int h, int slot, int kb) const {
+        return (bl(b, L) * n_kv + h) * (size_t)cap * cb_max + (size_t)slot * kb;
+    }
 };
 
 struct FullView {
@@ -554,7 +559,68 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
 
     int hwm = c.meta[bl * 4 + 0];
+    const int live0 = c.meta[bl * 4 + 1];
     const int trunc = a.trunc ? a.trunc[b] : -1;
+    const int R = a.n_rows ? a.n_rows[b] : a.src_rows_max;
+    const int p0 = a.pos0 ? a.pos0[b] : 0;
+    if (R > kAppendMaxRows || R > a.src_rows_max) {
+        if (tid == 0) atomicOr(a.err, 0x10u);
+        return;
+    }
+    // seen: clipped by truncation, advanced to the last appended position + 1
+    int seen = c.seen[b];
+    if (trunc >= 0 && trunc < seen) seen = trunc;
+    if (a.advance_seen && R > 0 && p0 + R > seen) seen = p0 + R;
+
+    // quantize + pack the R new rows into slot_list[0..R) (one warp per K or V vector)
+    const int d = c.d;
+    auto quantize_rows = [&]() {
+        uint8_t* scratch = ap_smem + wid * d;
+        const int n_vec = R * c.n_kv * 2;
+        const int kb = code_row_bytes(d, bits, a.raw_dtype);
+        for (int v = wid; v < n_vec; v += nw) {
+            const int r = v / (2 * c.n_kv);
+            const int h = (v / 2) % c.n_kv;
+            const bool is_k = (v & 1) == 0;
+            const int slot = slot_list[r];
+            const size_t vi = c.vec(b, L, h, slot);
+            uint8_t* dst = (is_k ? c.k_codes : c.v_codes) + c.code_off(b, L, h, slot, kb);
+            uint16_t* sl = (is_k ? c.k_sl : c.v_sl) + vi * (d / 64) * 2;
+            if (a.src) {
+                const size_t off = ((((size_t)b * a.rows_stride + r) * c.n_kv + h) * 2 + (is_k ? 0 : 1)) * d;
+                quant_pack_vector(a.src, a.src_dtype, off, d, bits, is_k, dst, sl, a.raw_dtype, scratch);
+            } else {
+                const size_t off = a.f.elem(b, L, h, p0 + r);
+                quant_pack_vector(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, off, d, bits, is_k, dst, sl,
+                                  a.raw_dtype, scratch);
+            }
+        }
+    };
+
+    // ---- fast path: nothing to truncate, no hole below hwm and keep >= 1
+    // (the budget, max(keep * seen, sink + recent), is never below the live
+    // count, so nothing is evicted): the rows go to hwm.. and the counts
+    // advance by R, exactly what the general path below computes then
+    if (trunc < 0 && live0 == hwm && keep >= 1.0) {
+        if (hwm + R > c.cap) {
+            if (tid == 0) atomicOr(a.err, 0x20u);
+            return;
+        }
+        for (int r = tid; r < R; r += blockDim.x) slot_list[r] = hwm + r;
+        __syncthreads();
+        quantize_rows();
+        for (int r = tid; r < R; r += blockDim.x) {
+            pos[hwm + r] = p0 + r;
+            score[hwm + r] = 0.f;
+        }
+        if (tid == 0) {
+            c.meta[bl * 4 + 0] = hwm + R;
+            c.meta[bl * 4 + 1] = live0 + R;
+            if (L == 0 && a.advance_seen) c.seen[b] = seen;
+        }
+        return;
+    }
+
     // positions of the slot array, staged in shared memory when they fit
     // (every pass below reads them; writes go to both copies)
     int32_t* spos = reinterpret_cast<int32_t*>(ap_smem + (size_t)nw * c.d);
@@ -583,16 +649,6 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
         for (int s = tid; s < hwm; s += blockDim.x)
             if (P[s] >= trunc) setp(s, -1);
     }
-    const int R = a.n_rows ? a.n_rows[b] : a.src_rows_max;
-    const int p0 = a.pos0 ? a.pos0[b] : 0;
-    if (R > kAppendMaxRows || R > a.src_rows_max) {
-        if (tid == 0) atomicOr(a.err, 0x10u);
-        return;
-    }
-    // seen: clipped by truncation, advanced to the last appended position + 1
-    int seen = c.seen[b];
-    if (trunc >= 0 && trunc < seen) seen = trunc;
-    if (a.advance_seen && R > 0 && p0 + R > seen) seen = p0 + R;
     __syncthreads();
 
     // ---- slots for the R new rows: the lowest R empty slots in slot order,
@@ -641,27 +697,8 @@ __global__ void __launch_bounds__(kAppendThreads) comp_append_kernel(AppendArgs 
         return;
     }
 
-    // ---- quantize + pack the new rows (one warp per K or V vector)
-    const int d = c.d;
-    uint8_t* scratch = ap_smem + wid * d;
-    const int n_vec = R * c.n_kv * 2;
-    for (int v = wid; v < n_vec; v += nw) {
-        const int r = v / (2 * c.n_kv);
-        const int h = (v / 2) % c.n_kv;
-        const bool is_k = (v & 1) == 0;
-        const int slot = slot_list[r];
-        const size_t vi = c.vec(b, L, h, slot);
-        uint8_t* dst = (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max;
-        uint16_t* sl = (is_k ? c.k_sl : c.v_sl) + vi * (d / 64) * 2;
-        if (a.src) {
-            const size_t off = ((((size_t)b * a.rows_stride + r) * c.n_kv + h) * 2 + (is_k ? 0 : 1)) * d;
-            quant_pack_vector(a.src, a.src_dtype, off, d, bits, is_k, dst, sl, a.raw_dtype, scratch);
-        } else {
-            const size_t off = a.f.elem(b, L, h, p0 + r);
-            quant_pack_vector(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, off, d, bits, is_k, dst, sl,
-                              a.raw_dtype, scratch);
-        }
-    }
+    // ---- quantize + pack the new rows
+    quantize_rows();
     for (int r = tid; r < R; r += blockDim.x) {
         setp(slot_list[r], p0 + r);
         score[slot_list[r]] = 0.f;
@@ -942,7 +979,7 @@ __global__ void comp_rebuild_kernel(RebuildArgs a) {
         const int p = s < gap_at ? s : s + gap_len;
         const size_t vi = c.vec(b, L, h, s);
         quant_pack_vector(is_k ? a.f.k_pool : a.f.v_pool, a.f.dtype, a.f.elem(b, L, h, p), d, bits, is_k,
-                          (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max,
+                          (is_k ? c.k_codes : c.v_codes) + c.code_off(b, L, h, s, code_row_bytes(d, bits, a.raw_dtype)),
                           (is_k ? c.k_sl : c.v_sl) + vi * (d / 64) * 2, a.raw_dtype, scratch);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -1012,7 +1049,8 @@ __global__ void __launch_bounds__(256) comp_rebuild_slice_kernel(RebuildArgs a) 
             const bool is_k = hk < c.n_kv;
             const int h = is_k ? hk : hk - c.n_kv;
             const size_t vi = c.vec(b, L, h, s);
-            quant_pack_slice(x[u], j, d, bits, is_k, act[u], (is_k ? c.k_codes : c.v_codes) + vi * c.cb_max,
+            quant_pack_slice(x[u], j, d, bits, is_k, act[u],
+                             (is_k ? c.k_codes : c.v_codes) + c.code_off(b, L, h, s, code_row_bytes(d, bits, a.raw_dtype)),
                              (is_k ? c.k_sl : c.v_sl) + vi * sl_stride, a.raw_dtype);
         }
     }
@@ -1046,8 +1084,9 @@ __global__ void comp_read_kernel(CompView c, int b, int L, int bits, int raw_dty
         const size_t vi = c.vec(b, L, h, slot);
         float kv = 0.f, vv = 0.f;
         if (p >= 0) {
-            kv = dequant_elem(c.k_codes + vi * c.cb_max, c.k_sl + vi * (d / 64) * 2, d, bits, true, e, raw_dtype);
-            vv = dequant_elem(c.v_codes + vi * c.cb_max, c.v_sl + vi * (d / 64) * 2, d, bits, false, e, raw_dtype);
+            const size_t co = c.code_off(b, L, h, slot, code_row_bytes(d, bits, raw_dtype));
+            kv = dequant_elem(c.k_codes + co, c.k_sl + vi * (d / 64) * 2, d, bits, true, e, raw_dtype);
+            vv = dequant_elem(c.v_codes + co, c.v_sl + vi * (d / 64) * 2, d, bits, false, e, raw_dtype);
         }
         k[((size_t)slot * c.n_kv + h) * d + e] = kv;
         v[((size_t)slot * c.n_kv + h) * d + e] = vv;

@@ -290,6 +290,16 @@ class CompressedKVCache:
         _lib.call("dkv_comp_append", self.struct(), None, self.dims(), layer, 1, src.data_ptr(), self.dtype, n,
                   p0.data_ptr(), nr.data_ptr(), None, 1 if layer == 0 else 0, _lib.stream_ptr())
 
+    def code_rows(self, which: str, layer: int, b: int = 0):
+        """Packed codes ("k" or "v") of one layer and sequence as a
+        [n_kv][cap][bytes per vector] view: a layer's vectors are stored
+        densely at the width of its current configuration inside each
+        (sequence, layer, head) region of the allocation."""
+        bits, d = self.cfgs[layer].bits, self.d_head
+        kb = d * (4 if self.cb_max >= d * 4 else 2) if bits >= 16 else d * bits // 8
+        t = getattr(self, which + "_codes")[b, layer]                # [n_kv][cap][cb_max]
+        return t.reshape(t.shape[0], -1)[:, : self.cap * kb].reshape(t.shape[0], self.cap, kb)
+
     def read(self, layer: int, b: int = 0):
         """Dequantized (k, v, pos) of the live entries in position order."""
         if not self._ready:

@@ -161,7 +161,7 @@ def test_rebuild_bytes_match_reference_packing(d, bits, dtype):
     for L in range(2):
         rk, rv, _ = ref.read(L)                                    # [n][n_kv][d]
         for name, x, k_order in (("k", rk, True), ("v", rv, False)):
-            codes = getattr(comp, name + "_codes")[0, L, :, :n].cpu().numpy()    # [n_kv][n][cb_max]
+            codes = comp.code_rows(name, L)[:, :n].cpu().numpy()                  # [n_kv][n][bytes]
             sl = getattr(comp, name + "_sl")[0, L, :, :n].cpu().numpy().view(np.float16)
             for h in range(n_kv):
                 if bits == 16:

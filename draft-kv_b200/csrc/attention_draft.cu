@@ -852,15 +852,19 @@ cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cudaStream
     cfg.blockDim = dim3(kDraftThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute at[2];
+    // No programmatic dependent launch: clusters placed early, while the
+    // previous kernel (the append) still holds a few SMs, can leave a
+    // cluster without room in its GPC until a whole first-wave cluster ends
+    // (measured on B200 in the decode round: CTAs starting up to 100 us late,
+    // the launch running in two waves).  The kernel's own griddepcontrol
+    // wait is then a no-op and its trigger still lets the next kernel start.
+    cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = da.cs;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, attn_draft_tc_kernel<D, BITS, NST>, da);
 }
 

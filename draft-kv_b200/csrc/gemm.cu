@@ -204,41 +204,6 @@ DKV_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)
 // X chunk row stride in bf16 elements (128 + 8 padding: conflict-free ldmatrix)
 constexpr int kXStride = kChunkK + 8;
 
-// ---- mbarrier / bulk-copy helpers (TMA without multicast)
-DKV_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-DKV_DEV void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
-}
-DKV_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-DKV_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-DKV_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-DKV_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait: gives up after ~2^22 polls (each poll may suspend briefly),
-// records 0x80 in the device error word and returns false.
-DKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-    for (uint32_t i = 0; i < (1u << 22); ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    if (err) atomicOr(err, 0x80u);
-    return false;
-}
-
 constexpr int kWChunkBytes = kChunkSteps * 512;   // one warp's weights for one X chunk
 
 // Weight stages per warp: deeper for few tokens (small X chunks).

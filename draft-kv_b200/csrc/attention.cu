@@ -364,6 +364,11 @@ extern "C" int dkv_attn_comp(const dkv_comp_cache* comp, dkv_dims dims, int laye
     a.scale = 1.0f / sqrtf((float)dims.d);
     a.mass = comp->mass;
     a.score = comp->score;
+    // A layer kept whole (keep >= 1) never evicts, and a configuration switch
+    // rebuilds the drafter cache at zero scores, so its accumulated mass is
+    // never read: the tensor-core kernel skips it (the generic kernel, for
+    // fp32 16-bit entries, still folds it).
+    a.note_mass = !(comp->keep && comp->keep[layer] >= 1.0);
     bool handled = false;
     // 16-bit entries are stored in the model dtype: 4-byte elements mean fp32
     const int raw_dtype = comp->cb_max >= dims.d * 4 ? DKV_F32 : DKV_BF16;

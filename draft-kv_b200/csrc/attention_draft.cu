@@ -162,6 +162,7 @@ struct DraftArgs {
                             // in shared memory [group][chunk_cap] after the region
     int raw_dtype;          // dtype of 16-bit entries
     int ch16;               // code rows are 16-byte aligned: 16-byte copies
+    int note_mass;          // keep the raw scores and fold the attention mass into the slot scores
     uint32_t* tickets;      // comp->tickets [batch][n_layers][64]
     uint32_t* err;
 };
@@ -324,8 +325,9 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     float* tailp = reinterpret_cast<float*>(dsm + da.region);
     // raw scores (log2 units) of this CTA's slots, slot-major:
     // sbuf[(s - s0) * G + g]
-    float* sbuf;
-    if (da.gsc) {
+    float* sbuf = nullptr;
+    if (!da.note_mass) {
+    } else if (da.gsc) {
         sbuf = da.gsc + (((size_t)b * a.n_kv + h) * (size_t)src.cap + s0) * G;
     } else {
         sbuf = tailp;
@@ -541,7 +543,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
                     if (h0 + 1 < G) p[1] = y;
                 }
             };
-            if (h0 < G) {
+            if (h0 < G && da.note_mass) {
                 if (ina && sa - s0 < cc) put(sa, sc[0], sc[1]);
                 if (inb && sb - s0 < cc) put(sb, sc[2], sc[3]);
             }
@@ -750,7 +752,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
     // ---- exact attention mass of this CTA's slots for head h (group sum)
     const int32_t* cpos = src.cpos + bl * src.cap;
     float* mass_h = a.mass + (bl * a.n_kv + h) * (size_t)src.cap;
-    for (int s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
+    for (int s = s0 + threadIdx.x; da.note_mass && s < s1; s += blockDim.x) {
         float mv = 0.f;
         if (s - s0 < cc) {
             const float* rp = sbuf + (size_t)(s - s0) * G;
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
         }
         mass_h[s] = mv;
     }
-    if (da.gsc) {
+    if (da.gsc && da.note_mass) {
         // the scores of [s0, s1) are consumed: drop their L2 lines without a
         // write-back (whole 128-byte lines inside the range only; the lines it
         // shares with the neighbouring ranges stay)
@@ -778,6 +780,7 @@ __global__ void __launch_bounds__(kDraftThreads, 2) attn_draft_tc_kernel(DraftAr
             asm volatile("discard.global.L2 [%0], 128;\n" ::"l"(q) : "memory");
     }
     cluster.sync();   // remote shared memory stays alive until every CTA has read it
+    if (!da.note_mass) return;
     // ---- fold the heads' masses into the scores of this slot range (head order)
     __threadfence();
     __syncthreads();
@@ -927,8 +930,9 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
         const int ctas = pairs * cs;
         for (int nst = 4; nst >= 2; --nst) {
             const size_t region = std::max((size_t)kDraftWarps * nst * shp.stage, (size_t)kDraftWarps * 8 * D * 4);
-            for (int gl = 0; gl < 2; ++gl) {
-                if (gl && !gsc) continue;
+            // gl = 2: no score buffer (the mass is not folded)
+            for (int gl = a.note_mass ? 0 : 2; gl < (a.note_mass ? 2 : 3); ++gl) {
+                if (gl == 1 && !gsc) continue;
                 const size_t smem = region + tail + (gl ? 0 : (size_t)a.group * chunk_cap * sizeof(float));
                 if (smem > kSmemLimit) continue;
                 // <= 128 registers a thread (launch bounds): two CTAs per SM
@@ -937,14 +941,14 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
                 const int waves = (ctas + 148 * per_sm - 1) / (148 * per_sm);
                 const int busy = std::min(per_sm, (ctas + 147) / 148);    // CTAs sharing an SM
                 const double cost = (double)waves * ((double)busy * chunk_cap * (nst == 2 ? 1.15 : 1.0) *
-                                                         (busy == 1 ? 1.5 : 1.0) * (gl ? 1.05 : 1.0) +
+                                                         (busy == 1 ? 1.5 : 1.0) * (gl == 1 ? 1.05 : 1.0) +
                                                      kFixedSlots);
                 if (best_cs == 0 || cost < best_cost - 1e-9) {
                     best_cost = cost;
                     best_cs = cs;
                     best_nst = nst;
                     best_cap = chunk_cap;
-                    best_gl = gl != 0;
+                    best_gl = gl == 1;
                     best_smem = smem;
                     best_region = region;
                 }
@@ -960,6 +964,7 @@ int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cuda
     da.gsc = best_gl ? gsc : nullptr;
     da.raw_dtype = raw_dtype;
     da.ch16 = a.src.cb_max % 16 == 0;
+    da.note_mass = a.note_mass;
     da.tickets = comp_tickets;
     da.err = device_error_word();
     da.a.src.dtype = raw_dtype;

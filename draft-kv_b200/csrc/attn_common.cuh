@@ -39,6 +39,7 @@ struct AttnArgs {
     unsigned* tickets;       // [batch][n_kv][n_rb]  (+ [batch] head tickets for the fold)
     float* sbuf;             // drafter: raw scores [batch][n_kv][group][cap]
     float* mass;             // drafter: [batch][n_layers][n_kv][cap]
+    int note_mass;           // drafter: fold the attention mass into the slot scores
     float* score;            // drafter: [batch][n_layers][cap]
     unsigned* fold_tickets;  // [batch]
 };

@@ -102,6 +102,14 @@ typedef struct {
     int n_pages, page_size, max_pages, dtype;
 } dkv_full_cache;
 
+/* Drafter cache (slot arrays).  k_codes / v_codes: batch x n_layers x n_kv
+ * regions of cap * cb_max bytes; a layer's vectors are stored densely inside
+ * its region at the width of its current configuration (d*bits/8 bytes,
+ * 16-bit entries d * element size), slot s at byte s * width.  k_sl / v_sl:
+ * per vector and 64-group fp16 (scale, lo).  pos: batch x n_layers x cap
+ * (-1 = empty); score (H2O, accumulated only for layers with keep < 1) and
+ * mass: batch x n_layers [x n_kv] x cap; meta: {high-water mark, live count,
+ * -, -} per (sequence, layer); cap is a multiple of 16. */
 typedef struct {
     uint8_t* k_codes;
     uint8_t* v_codes;

@@ -333,6 +333,50 @@ def test_draft_attention_and_mass(bits, d, dtype):
         np.testing.assert_allclose(got, mass, atol=1e-3, rtol=3e-2)
 
 
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("d", [64, 128])
+def test_draft_attention_keep_whole_skips_scores(bits, d):
+    """A layer kept whole (keep 1.0) never evicts, so the tensor-core drafter
+    kernel does not fold the attention mass into the slot scores: the output
+    still matches a torch fp32 reference on the read-back entries (2e-2 of
+    the output scale, f16 operands) and the scores are left as they were."""
+    from draftkv import CompressedKVCache, FullKVCache
+    L = lib()
+    B, n_kv, G, n = 2, 2, 4, 700
+    full = FullKVCache(1, n_kv, d, "bf16", capacity=n + 16, batch=B)
+    rng = np.random.default_rng(bits * 11 + d)
+    for b in range(B):
+        full.ensure(b, n)
+    k = round_bf16(rng.standard_normal((B, n, n_kv, d)).astype(np.float32))
+    v = round_bf16(rng.standard_normal((B, n, n_kv, d)).astype(np.float32))
+    src = torch.from_numpy(np.stack([k, v], axis=3)).to("cuda", torch.bfloat16)
+    p0 = torch.zeros((B,), dtype=torch.int32, device="cuda")
+    L.call("dkv_full_write", full.struct(), full.dims(), 0, src.data_ptr(), n, p0.data_ptr(), None, L.stream_ptr())
+    for b in range(B):
+        full.set_length(b, n)
+    comp = CompressedKVCache(1, CompressionConfig(bits, 1.0), n_kv=n_kv, d_head=d, dtype="bf16",
+                             capacity=n + 8, batch=B)
+    comp.sync_from(full, 0)
+    comp.score_t.copy_(torch.rand_like(comp.score_t))
+    q = torch.from_numpy(rng.standard_normal((B, n_kv * G, d)).astype(np.float32) * 2).cuda()
+    qpos = torch.full((B,), n, dtype=torch.int32, device="cuda")
+    out = torch.zeros((B, n_kv * G * d), dtype=torch.float32, device="cuda")
+    dims = comp.dims()
+    work = torch.zeros(int(L.load().dkv_attn_work_bytes(dims, G, 1, 16, 512, comp.cap)), dtype=torch.uint8,
+                       device="cuda")
+    before = comp.score_t.clone()
+    L.call("dkv_attn_comp", comp.struct(), dims, 0, G, q.data_ptr(), qpos.data_ptr(), out.data_ptr(), L.F32,
+           work.data_ptr(), work.numel(), L.stream_ptr())
+    assert torch.equal(comp.score_t, before)
+    for b in range(B):
+        kk, vv, _ = comp.read(0, b)
+        kt = torch.from_numpy(kk).cuda().repeat_interleave(G, dim=1)
+        vt = torch.from_numpy(vv).cuda().repeat_interleave(G, dim=1)
+        s_ = torch.einsum("hd,khd->hk", q[b], kt) / np.sqrt(d)
+        ref = torch.einsum("hk,khd->hd", torch.softmax(s_, -1), vt).reshape(-1)
+        assert (out[b] - ref).abs().max().item() <= 2e-2 * ref.abs().max().item(), b
+
+
 # ------------------------------------------------------------- K3
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("G", [1, 4])

@@ -88,7 +88,10 @@ def model_config(name: str) -> dict:
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) during the timed region."""
+    """nvidia-smi samples (every 50 ms) during the timed region.  start()
+    returns once the sampler is live (its first line has arrived); only lines
+    that arrive after the mark set at the start of the timed region count, so
+    a short timed region still gets its own samples."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -99,17 +102,22 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.mark = 0
 
     def start(self) -> None:
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        t0 = time.perf_counter()
+        while not self.lines and time.perf_counter() - t0 < 5.0:
+            time.sleep(0.01)
+        self.mark = len(self.lines)
 
     def _read(self) -> None:
         for line in self.proc.stdout:
@@ -127,7 +135,8 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        during = self.lines[self.mark:] or self.lines[-1:]      # the last sample before, if none during
+        for ln in during:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -140,7 +149,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=mx, reasons=sorted(reasons),
-                    samples=len(sm))
+                    samples=len(sm), during=len(self.lines) > self.mark)
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -343,13 +352,16 @@ def run_gpu(args) -> None:
         cfgs = {}
         gammas = []
         dbytes = 0.0       # algorithmic drafter-attention bytes of the rounds (per config used)
+        # the clock sampler is live before the barrier, so every rank enters
+        # the timed region together
+        clk = ClockSampler(local)
+        clk.start()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         if profile:
             _lib.call("dkv_prof_start", 400000)
-        clk = ClockSampler(local)
-        clk.start()
+        clk.mark = len(clk.lines)
         t0 = time.perf_counter()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)

@@ -272,14 +272,32 @@ def run_gpu(args) -> None:
     pk = peaks()
     t_setup = time.perf_counter()
     wts = random_device_weights(cfg, seed=0, std=0.02)
-    # keys per attention split: fixed for the model (verify and decode rows
-    # then share split boundaries); ctx / 8 keeps 8 splits per (sequence,
-    # head) in flight while each split streams long enough to amortise its
-    # merge (measured on B200: 4096-key splits at ctx 32768 run verify
-    # attention 1.4-1.6x faster than 512-key splits)
-    split = 512
-    while split * 2 <= min(4096, ctx // 8):
-        split *= 2
+    # keys per attention split: fixed for the model for the whole run (verify
+    # and decode rows then share split boundaries).  When the (sequence, KV
+    # head) pairs fit two CTAs per SM, the run's longest context is cut into
+    # as many equal 64-key-aligned splits as keep one wave of two CTAs per
+    # SM (measured on B200, batch 4 at ctx 33600: 3776-key splits 129 us
+    # against 135 us for 4096-key ones, whose last split is nearly empty);
+    # otherwise ctx / 8, a power of two from 512 to 4096, keeps 8 splits per
+    # pair in flight while each streams long enough to amortise its merge.
+    # controller settle: untimed rounds after the warm-up in which the
+    # Thompson controller explores its arms (its posterior starts flat); the
+    # timed rounds then measure the steady state it converges to.  The settle
+    # rounds are timed on their own and reported as "explore".
+    settle = 0 if "fixed" in conf else args.settle
+    rounds_needed = args.warmup + settle + 2 * args.steps + 13     # + timed, profiled, baseline rounds
+    max_new = rounds_needed * (G + 1) + 8
+    n_kv_heads = cfg.get("num_key_value_heads", cfg.get("n_head", 1))
+    pairs = B * n_kv_heads
+    if args.split_keys:
+        split = args.split_keys
+    elif pairs <= 148:
+        n_split = max(1, (2 * 148) // pairs)
+        split = -(-(ctx + max_new) // (n_split * 64)) * 64
+    else:
+        split = 512
+        while split * 2 <= min(4096, ctx // 8):
+            split *= 2
     model = from_config(wts, cfg, split_keys=split)
     del wts
     torch.cuda.empty_cache()
@@ -313,15 +331,8 @@ def run_gpu(args) -> None:
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
     engine.offload_full = bool(conf.get("offload"))
-    # controller settle: untimed rounds after the warm-up in which the
-    # Thompson controller explores its arms (its posterior starts flat); the
-    # timed rounds then measure the steady state it converges to.  The settle
-    # rounds are timed on their own and reported as "explore".
-    settle = 0 if "fixed" in conf else args.settle
-    rounds_needed = args.warmup + settle + 2 * args.steps + 13     # + timed, profiled, baseline rounds
     vocab = model.vocab_size
     prompts = [[int(x) for x in np.random.default_rng(1 + 1000 * rank + b).integers(0, vocab, ctx)] for b in range(B)]
-    max_new = rounds_needed * (G + 1) + 8
     sess = engine.session(prompts, max_new, T, exchange=exchange)
     torch.cuda.synchronize()
     setup_s = time.perf_counter() - t_setup
@@ -408,7 +419,7 @@ def run_gpu(args) -> None:
     saved_ctrl, saved_comp = engine.controller, sess.st.comp
     engine.controller = FixedPolicy(CompressionConfig(16, 1.0), 0)
     sess.st.comp = None
-    base_steps = max(3, min(args.steps, 8))
+    base_steps = max(3, min(args.steps, 20))    # ~150 ms of plain decode rounds (8 were noisy)
     sess.round()
     btoks, bdev_s, bwall_s, _, _, _, _ = timed_rounds(base_steps, profile=False)
     engine.controller, sess.st.comp = saved_ctrl, saved_comp
@@ -669,6 +680,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--settle", type=int, default=60,
                     help="untimed controller-settle rounds after the warm-up (Thompson-controlled configs)")
+    ap.add_argument("--split-keys", type=int, default=0,
+                    help="keys per attention split (multiple of 64; default: chosen from the shape)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "gemm"], default=None,
                     help="time one kernel alone on a synthetic case instead of the decode step")

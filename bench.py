@@ -152,6 +152,20 @@ class ClockSampler:
                     samples=len(sm), during=len(self.lines) > self.mark)
 
 
+def attention_split(ctx: int, ctx_max: int, pairs: int, sms: int = 148) -> int:
+    """Keys per attention split for a run whose context grows from ctx to
+    ctx_max with `pairs` (sequence, KV head) pairs: equal 64-key-aligned
+    splits of ctx_max, as many as keep one wave of two CTAs per SM, when the
+    pairs allow it; otherwise ctx / 8 as a power of two from 512 to 4096."""
+    if pairs <= sms:
+        n_split = max(1, (2 * sms) // pairs)
+        return -(-ctx_max // (n_split * 64)) * 64
+    split = 512
+    while split * 2 <= min(4096, ctx // 8):
+        split *= 2
+    return split
+
+
 # ---------------------------------------------------------------- CPU baseline
 def cpu_baseline(cfg: dict, ctx: int, gamma: int, tokens_per_round: float | None, bits: int, keep: float,
                  budget_s: float = 25.0) -> dict:
@@ -289,15 +303,7 @@ def run_gpu(args) -> None:
     max_new = rounds_needed * (G + 1) + 8
     n_kv_heads = cfg.get("num_key_value_heads", cfg.get("n_head", 1))
     pairs = B * n_kv_heads
-    if args.split_keys:
-        split = args.split_keys
-    elif pairs <= 148:
-        n_split = max(1, (2 * 148) // pairs)
-        split = -(-(ctx + max_new) // (n_split * 64)) * 64
-    else:
-        split = 512
-        while split * 2 <= min(4096, ctx // 8):
-            split *= 2
+    split = args.split_keys or attention_split(ctx, ctx + max_new, pairs)
     model = from_config(wts, cfg, split_keys=split)
     del wts
     torch.cuda.empty_cache()

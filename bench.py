@@ -270,6 +270,9 @@ def run_gpu(args) -> None:
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
+        # NCCL's own messages (its version banner included) go to stderr:
+        # rank 0's stdout carries the one JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     from draftkv import (CompressionConfig, CostModel, DraftKVEngine, FixedPolicy, LlamaLike, ThompsonController,

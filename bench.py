@@ -260,9 +260,21 @@ def cpu_baseline(cfg: dict, ctx: int, gamma: int, tokens_per_round: float | None
 
 
 # ---------------------------------------------------------------- GPU run
+def json_stdout():
+    """A private handle on the process's real stdout for the one JSON line;
+    file descriptor 1 itself is pointed at stderr, so anything else written
+    there (a communication library's banner, say) cannot join the line."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
+
+    out = json_stdout()
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -270,9 +282,6 @@ def run_gpu(args) -> None:
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        # NCCL's own messages (its version banner included) go to stderr:
-        # rank 0's stdout carries the one JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
 
     from draftkv import (CompressionConfig, CostModel, DraftKVEngine, FixedPolicy, LlamaLike, ThompsonController,
@@ -534,7 +543,7 @@ def run_gpu(args) -> None:
         "setup_s": round(setup_s, 1),
     }
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -293,11 +293,7 @@ static int launch_generic(AttnArgs& a, dkv_dims dims, void* work, size_t work_by
                 "attention: work buffer too small (%zu bytes)", work_bytes);
     const size_t smem = generic_smem(R < kGenRB ? R : kGenRB, dims.d);
     DKV_REQUIRE(smem <= 220 * 1024, "attention: %zu bytes of shared memory", smem);
-    static bool attr = false;
-    if (!attr) {
-        DKV_CUDA(allow_smem_max(attn_generic_kernel));
-        attr = true;
-    }
+    DKV_CUDA(allow_smem_max_once<attn_generic_kernel>());
     dim3 grid(a.n_splits, dims.n_kv, dims.batch * a.n_rb);
     {
         ProfScope ps(comp ? DKV_PROF_ATTN_COMP : DKV_PROF_ATTN_FULL, 0.0, st);

@@ -838,18 +838,14 @@ DraftShape draft_shape() {
 
 template <int D, int BITS, int NST>
 cudaError_t launch_draft(const DraftArgs& da, dim3 grid, size_t smem, cudaStream_t st) {
-    static int attr_dev = -1;     // attributes are per device
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static DeviceOnce once;     // attributes are per device
+    cudaError_t e = once.run([] {
+        cudaError_t r = allow_smem_max(attn_draft_tc_kernel<D, BITS, NST>);
+        if (r != cudaSuccess) return r;
+        return cudaFuncSetAttribute(attn_draft_tc_kernel<D, BITS, NST>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                                    1);
+    });
     if (e != cudaSuccess) return e;
-    if (attr_dev != dev) {
-        e = allow_smem_max(attn_draft_tc_kernel<D, BITS, NST>);
-        if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(attn_draft_tc_kernel<D, BITS, NST>, cudaFuncAttributeNonPortableClusterSizeAllowed,
-                                 1);
-        if (e != cudaSuccess) return e;
-        attr_dev = dev;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kDraftThreads);

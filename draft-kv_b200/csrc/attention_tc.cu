@@ -489,15 +489,8 @@ size_t full_tc_smem() {
 
 template <int D, int MAXT>
 cudaError_t launch_kq(const AttnArgs& a, dim3 grid, int threads, cudaStream_t st) {
-    static int attr_dev = -1;     // attributes are per device
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    const cudaError_t e = allow_smem_max_once<attn_kq_kernel<D, MAXT>>();
     if (e != cudaSuccess) return e;
-    if (attr_dev != dev) {
-        e = allow_smem_max(attn_kq_kernel<D, MAXT>);
-        if (e != cudaSuccess) return e;
-        attr_dev = dev;
-    }
     return launch_pdl(attn_kq_kernel<D, MAXT>, grid, dim3(threads), kq_smem<D>((threads / 32) / kKqKG), st, a);
 }
 
@@ -540,18 +533,10 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
         return DKV_OK;
     }
     if (dims.d == 128) {
-        static bool attr = false;
-        if (!attr) {
-            DKV_CUDA(allow_smem_max(attn_full_tc_kernel<128>));
-            attr = true;
-        }
+        DKV_CUDA(allow_smem_max_once<attn_full_tc_kernel<128>>());
         attn_full_tc_kernel<128><<<grid, kTcThreads, full_tc_smem<128>(), st>>>(a);
     } else {
-        static bool attr = false;
-        if (!attr) {
-            DKV_CUDA(allow_smem_max(attn_full_tc_kernel<64>));
-            attr = true;
-        }
+        DKV_CUDA(allow_smem_max_once<attn_full_tc_kernel<64>>());
         attn_full_tc_kernel<64><<<grid, kTcThreads, full_tc_smem<64>(), st>>>(a);
     }
     DKV_LAUNCHED();

@@ -1,6 +1,7 @@
 // Shared helpers for the draftkv_b200 kernels (sm_100a).
 #pragma once
 
+#include <atomic>
 #include <utility>
 
 #include <cuda_runtime.h>
@@ -69,6 +70,36 @@ inline cudaError_t allow_smem_max(K kernel) {
     if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+}
+
+// Once-per-device set-up (kernel attributes such as the shared-memory limit
+// apply to the current device only, so every device needs its own call).
+// run(fn) calls fn() the first time it is reached with a given current device
+// and remembers a success; two threads racing on the first call may both run
+// fn, which must therefore be idempotent.  Devices beyond 63 run fn on every
+// call.  A cudaDeviceReset() discards the attributes but not these flags:
+// calls must not cross a reset of a device they have already used.
+struct DeviceOnce {
+    std::atomic<uint64_t> done{0};
+    template <typename F>
+    cudaError_t run(F&& fn) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+        if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+        e = fn();
+        if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+        return e;
+    }
+};
+
+// allow_smem_max(Kern) once per device (one flag set per kernel: the kernel
+// is a template argument, not a runtime value).
+template <auto Kern>
+inline cudaError_t allow_smem_max_once() {
+    static DeviceOnce once;
+    return once.run([] { return allow_smem_max(Kern); });
 }
 
 // Programmatic dependent launch.  A kernel launched with launch_pdl() may

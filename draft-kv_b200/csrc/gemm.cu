@@ -819,11 +819,7 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
         DKV_REQUIRE(act > 0, "dkv_gemm: no resident cluster of %d CTAs", S);            \
         const int ncl = cl_count(mtiles, act);                                          \
         if (S == 1 && ncl == mtiles) {                                                  \
-            static bool attr = false;                                                   \
-            if (!attr) {                                                                \
-                DKV_CUDA(allow_smem_max(gemm_bf16_kernel<NTV>));                        \
-                attr = true;                                                            \
-            }                                                                           \
+            DKV_CUDA(allow_smem_max_once<gemm_bf16_kernel<NTV>>());                     \
             DKV_CUDA(launch_pdl(gemm_bf16_kernel<NTV>, grid, dim3(256), gemm_smem<NTV>(), st, g)); \
         } else {                                                                        \
             DKV_CUDA(launch_cl(gemm_bf16_cl_kernel<NTV>, ncl, S, nblk, gemm_smem<NTV>(), st, g)); \
@@ -937,12 +933,15 @@ extern "C" int dkv_gemm_noalloc(const void* x, int x_dtype, const void* w, int w
     }
     if (N == 0) return DKV_OK;
     const int mtiles = M / kTileM;
-    const int S = choose_split(M, K);
+    // the same K split as dkv_gemm, so both sum the same partials in the same
+    // order and give bit-identical results
+    const int S = w_dtype == DKV_F32 ? choose_split(M, K) : choose_split_cl(M, K);
     const int tok = w_dtype == DKV_F32 ? kF32Tok : 64;
     const int nblk = (N + tok - 1) / tok;
     const size_t tickets = (size_t)nblk * mtiles;
     const size_t partial_bytes = S > 1 ? tickets * S * tok * kTileStride * sizeof(float) : 0;
-    DKV_REQUIRE(tickets * sizeof(unsigned) <= kNoAllocTicketBytes,
+    // an unsplit launch touches neither the tickets nor the partials
+    DKV_REQUIRE(S == 1 || tickets * sizeof(unsigned) <= kNoAllocTicketBytes,
                 "dkv_gemm_noalloc: %zu row tiles x token blocks exceed the %zu tickets of the fixed scratch "
                 "(use dkv_gemm with a work buffer)", tickets, kNoAllocTicketBytes / sizeof(unsigned));
     DKV_REQUIRE(partial_bytes <= kNoAllocBytes - kNoAllocTicketBytes,

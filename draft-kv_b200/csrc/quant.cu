@@ -73,8 +73,10 @@ __global__ void quantize_exact_kernel(const float* __restrict__ x, int64_t rows,
 }
 
 // --------------------------------------------------------------------------
-// Storage order of the drafter cache (see oracle/quant.py): K vectors in the
-// tensor-core fragment order, V vectors in element order.
+// Storage order of the drafter cache (stated with the bit layouts in
+// include/draftkv_b200.h): K vectors in the tensor-core fragment order, V
+// vectors in element order.  Storage position p of a K vector holds element
+// 16j + 2c + (r & 1) + 8 (r >> 1) for quad c = p / (d/4), k-step j and r = p % 4.
 DKV_DEV int storage_elem(int p, int d, bool k_order) {
     if (!k_order) return p;
     const int q4 = d >> 2;
@@ -1248,18 +1250,15 @@ extern "C" int dkv_comp_append(const dkv_comp_cache* comp, const dkv_full_cache*
     a.err = device_error_word();
     DKV_TRY(fill_cfgs(comp, nullptr, n_layer_sel, layer0, dims.d, raw_dtype == DKV_F32 ? 4 : 2, &a.cfg));
     // quantization scratch, plus the slot positions when they fit
-    static int attr_dev = -1;
-    static size_t smem_cap = 0;
-    int dev = 0;
-    DKV_CUDA(cudaGetDevice(&dev));
-    if (attr_dev != dev) {
-        DKV_CUDA(allow_smem_max(comp_append_kernel));
-        int optin = 0;
+    DKV_CUDA(allow_smem_max_once<comp_append_kernel>());
+    size_t smem_cap = 0;
+    {
+        int dev = 0, optin = 0;
+        DKV_CUDA(cudaGetDevice(&dev));
         DKV_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         cudaFuncAttributes fa;
         DKV_CUDA(cudaFuncGetAttributes(&fa, comp_append_kernel));
         smem_cap = (size_t)optin - fa.sharedSizeBytes;
-        attr_dev = dev;
     }
     size_t smem = (kAppendThreads / 32) * dims.d;
     a.stage_pos = smem + (size_t)comp->cap * sizeof(int32_t) <= smem_cap;

@@ -11,7 +11,10 @@
  *     message of the last failure on the calling thread is dkv_last_error();
  *     no C++ exception crosses this boundary;
  *   - pointers named d_* are device pointers; everything is caller-owned
- *     (the library never allocates device memory and never frees);
+ *     (the library never allocates device memory and never frees; the one
+ *     exception is the fixed DKV_GEMM_NOALLOC_SCRATCH_BYTES array that the
+ *     library image itself holds on every GPU that loads it, see
+ *     dkv_gemm_noalloc);
  *   - `stream` is a cudaStream_t passed as void*; all work is stream-ordered,
  *     no function synchronizes the host unless documented;
  *   - the library only launches kernels, so a sequence of calls may be
@@ -34,9 +37,23 @@
  *       seen             [batch]                  int32 logical context length
  *       tickets          [batch][n_layers][64]    uint32, zero at creation
  *     a layer of `bits` uses cb = d*bits/8 bytes per vector (16 bits: the
- *     vector stored unquantized in the model dtype, cb = d*elem).  K codes are
- *     stored in the fragment order, V codes in element order (see
- *     oracle/quant.py for the bit layout of each width).
+ *     vector stored unquantized in the model dtype, cb = d*elem).
+ *
+ * Code order and bit layout of one packed vector (d a multiple of 64; codes
+ * are the unsigned q of the quantizer, one fp16 (scale, lo) pair per group of
+ * 64 elements in element order):
+ *   storage order -- V vectors: element order.  K vectors: the tensor-core
+ *     fragment order: for lane quad c = 0..3 and k-step j = 0..d/16-1 the four
+ *     elements 16j+2c, 16j+2c+1, 16j+2c+8, 16j+2c+9 follow each other; quad c
+ *     owns one contiguous quarter of the vector, k-steps in order;
+ *   8 bits: one byte per code, in storage order;
+ *   4 bits: each 32-bit little-endian word holds 8 codes of storage positions
+ *     8w..8w+7: position 8w+2i at bits [4i, 4i+4), 8w+2i+1 at [16+4i, 20+4i);
+ *   2 bits: each word holds 16 codes: 16w+2i at bits [2i, 2i+2), 16w+2i+1 at
+ *     [16+2i, 18+2i);
+ *   3 bits: two planes: plane A (d/4 bytes) holds every code's low two bits in
+ *     the 2-bit layout; plane B (d/8 bytes) follows and holds the high bits,
+ *     16 codes per 16-bit unit: position 16u+2i at bit i, 16u+2i+1 at 8+i.
  */
 #ifndef DRAFTKV_B200_H
 #define DRAFTKV_B200_H
@@ -90,7 +107,8 @@ DKV_API int dkv_quantize(const float* d_x, int64_t rows, int d, int bits, uint8_
 
 /* Packs rows into the drafter storage format: codes in the K (fragment) or V
  * (element) order and fp16 (scale, lo).  src [rows][d] in `src_dtype`.
- * Used by tests to check the kernel's bytes against oracle/quant.pack_codes. */
+ * The bytes follow the code order and bit layout stated at the top of this
+ * file (the tests check them against an independent packing). */
 DKV_API int dkv_quantize_pack(const void* d_src, int src_dtype, int64_t rows, int d, int bits,
                       int k_order, uint8_t* d_codes, uint16_t* d_sl, void* stream);
 
@@ -238,20 +256,27 @@ typedef struct {
  * fragments.  f32 weights are used as-is ([M][K] row-major). */
 DKV_API int dkv_pack_weight(const uint16_t* d_w, int M, int K, uint16_t* d_tiled, void* stream);
 
+/* The work buffer (dkv_gemm_work_bytes) must be zero when first used: the
+ * split-K arrival tickets live in it and every call leaves them zero again.
+ * One buffer must not serve calls that may run at the same time (different
+ * streams without ordering). */
 DKV_API int dkv_gemm(const void* d_x, int x_dtype, const void* d_w, int w_dtype, int M, int N, int K,
              const dkv_epilogue* epi, void* d_work, size_t work_bytes, void* stream);
 DKV_API size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype);
 
 /* dkv_gemm for callers that cannot allocate device memory: no counterpart in
- * the reference (which has no native code).  Same arguments and results as
- * dkv_gemm minus the work buffer; the split-K scratch is a fixed array of
- * DKV_GEMM_NOALLOC_SCRATCH_BYTES compiled into the library, held on every
- * GPU that loads it until the process exits.  Shapes whose split-K scratch
- * exceeds it return DKV_EINVAL with a message (e.g. 4096 x 4096 at 320
- * tokens; every weight of an 8B-class model fits at up to 64 tokens).
- * Allocates nothing.  The first call on a device does that device's set-up;
- * make it outside stream capture.  All calls on a device share the array:
- * calls that overlap on the GPU race. */
+ * the reference (which has no native code).  Same arguments as dkv_gemm minus
+ * the work buffer, and bit-identical results (the same K split, partials
+ * summed in the same order); the split-K scratch is a fixed array of
+ * DKV_GEMM_NOALLOC_SCRATCH_BYTES compiled into the library, held on every GPU
+ * that loads it until the process exits.  Split shapes whose scratch exceeds
+ * it return DKV_EINVAL with a message (e.g. 4096 x 4096 at 320 tokens; every
+ * weight of an 8B-class model fits at up to 64 tokens); unsplit shapes use
+ * no scratch and have no such limit.  Allocates nothing.  The first call on
+ * a device does that device's set-up (the array's device address, kernel
+ * attributes); make it outside stream capture, and do not call across a
+ * cudaDeviceReset() of a device already used.  All calls on a device share
+ * the array: calls that overlap on the GPU race. */
 #define DKV_GEMM_NOALLOC_SCRATCH_BYTES (16u << 20)
 DKV_API int dkv_gemm_noalloc(const void* d_x, int x_dtype, const void* d_w, int w_dtype, int M, int N, int K,
                              const dkv_epilogue* epi, void* stream);

@@ -355,7 +355,7 @@ def run_gpu(args) -> None:
     settle = 0 if "fixed" in conf else args.settle
     timed_n = args.steps * R
     prof_n = min(timed_n, args.prof_rounds)
-    spec_rounds = args.warmup * R + settle + timed_n + prof_n
+    spec_rounds = args.warmup * R + settle + timed_n + prof_n + 8      # + calibration rounds
     max_new = spec_rounds * (G + 1) + 8
     # keys per attention split: fixed for the model for the whole run (verify
     # and decode rows then share split boundaries).  When the (sequence, KV
@@ -409,6 +409,31 @@ def run_gpu(args) -> None:
 
     for _ in range(args.warmup * R):
         sess.round()
+    # CostModel constants measured on this device (a few real rounds at a
+    # fixed arm, part of the warm-up), then the controller built on them; the
+    # constants are averaged over ranks so replicated controllers stay equal
+    calib = None
+    if "fixed" not in conf and not args.no_calibrate:
+        from draftkv.calibrate import calibrate_cost_model
+        cm_cal, calib = calibrate_cost_model(sess, cm, CompressionConfig(8, 1.0), 2)
+        if world > 1:
+            v = torch.tensor([cm_cal.fixed_draft, cm_cal.fixed_verify, cm_cal.resync_per_token,
+                              cm_cal.rebuild_per_token or 0.0], dtype=torch.float64, device="cuda")
+            dist.all_reduce(v, op=dist.ReduceOp.SUM)
+            v = (v / world).tolist()
+            from dataclasses import replace
+            cm_cal = replace(cm_cal, fixed_draft=v[0], fixed_verify=v[1], resync_per_token=v[2],
+                             rebuild_per_token=v[3] or None)
+        arms = [CompressionConfig(b, k) for b, k in conf["arms"]] if "arms" in conf else default_arms()
+        ctrl = ThompsonController(cm_cal, arms, gamma_max=G, seed=0)
+        engine.controller = ctrl
+        calib = {k: (round(v, 9) if isinstance(v, float) else v) for k, v in calib.items()}
+        calib.update({"used": {"fixed_draft": cm_cal.fixed_draft, "fixed_verify": cm_cal.fixed_verify,
+                               "resync_per_token": cm_cal.resync_per_token,
+                               "rebuild_per_token": cm_cal.rebuild_per_token},
+                      "defaults": {"fixed_draft": cm.fixed_draft, "fixed_verify": cm.fixed_verify,
+                                   "resync_per_token": cm.resync_per_token},
+                      "ceiling_4b_keep0.25": round(cm_cal.ceiling(CompressionConfig(4, 0.25), ctx), 4)})
     explore = None
     if settle:
         torch.cuda.synchronize()
@@ -609,6 +634,7 @@ def run_gpu(args) -> None:
                    **({"h2d_gbs": round(h2d_bw / 1e9, 1)} if h2d_bw else {})},
         "lossless": lossless,
         "lossless_tokens_compared": compared,
+        "cost_model_calibration": calib,
         "controller_settle_rounds": settle,
         "explore": ({"rounds": explore["rounds"], "tokens_per_s": explore["tokens_per_s"],
                      "speedup_vs_full_kv": round(explore["tokens_per_s"] / base_tps, 4)} if explore else None),
@@ -765,6 +791,10 @@ def run_kernel(args) -> None:
         ts = []
         for _ in range(iters):
             flush.zero_()
+            # ~50 us of device time so that the host has queued the launch
+            # before the first event fires: the events then bracket device
+            # time only, not the host's submission latency
+            torch.cuda._sleep(100_000)
             a = torch.cuda.Event(enable_timing=True)
             b_ = torch.cuda.Event(enable_timing=True)
             a.record()
@@ -831,8 +861,7 @@ def run_kernel(args) -> None:
         M, K, N = args.M, args.K, args.N
         g = torch.Generator(device="cuda").manual_seed(0)
         W = (torch.randn((M, K), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-        Wt = torch.empty_like(W)
-        _lib.call("dkv_pack_weight", W.data_ptr(), M, K, Wt.data_ptr(), _lib.stream_ptr())
+        Wt = _lib.pack_weight(W)
         del W
         X = torch.randn((N, K), generator=g, device="cuda").to(torch.bfloat16)
         out = torch.zeros((N, M), dtype=torch.float32, device="cuda")
@@ -850,7 +879,8 @@ def run_kernel(args) -> None:
     gbs = by / (us * 1e-6) / 1e9
     line.update({"us": round(us, 2), "algorithmic_bytes": int(by), "achieved_gbs": round(gbs, 1),
                  "peak_gbs": round(pk["hbm_gbs"], 1), "frac": round(gbs / pk["hbm_gbs"], 4),
-                 "peak_source": pk["source"], "l2": "flushed between launches (256 MB write)"})
+                 "peak_source": pk["source"], "l2": "flushed between launches (256 MB write)",
+                 "timing": "CUDA events on the launching stream, queued behind a device-side sleep (device time only)"})
     print(json.dumps(line), flush=True)
 
 
@@ -872,6 +902,8 @@ def main() -> None:
     ap.add_argument("--split-keys", type=int, default=0,
                     help="keys per attention split (multiple of 64; default: chosen from the shape)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-calibrate", action="store_true",
+                    help="keep the cost model's default fixed costs instead of measuring them on the device")
     ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "gemm"], default=None,
                     help="time one kernel alone on a synthetic case instead of the decode step")
     ap.add_argument("--bits", type=int, default=4)

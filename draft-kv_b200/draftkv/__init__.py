@@ -15,6 +15,8 @@ from .controller import (DepthThompsonController, FixedPolicy, FlatBandit,
 from .throughput import (CostModel, best_gamma, best_gamma_profile, expected_tokens,
                          expected_tokens_profile)
 from .paged import BlockPool, BlockPoolExhausted, PagedKVCache, plan_blocks_needed
+from .adaptive import AdaptiveLayerController
+from .layers import SensitivityProfile, allocate
 from ._lib import DraftKVError
 
 _DEVICE_NAMES = {
@@ -33,6 +35,7 @@ def __getattr__(name):
 
 
 __all__ = [
+    "AdaptiveLayerController", "SensitivityProfile", "allocate",
     "BlockPool", "BlockPoolExhausted", "CompressedKVCache", "CompressionConfig", "CostModel",
     "DepthThompsonController", "DraftKVEngine", "DraftKVError", "FixedPolicy", "FlatBandit",
     "FullKVCache", "GPT2", "GenerationResult", "LayerPlan", "LlamaLike", "OraclePolicy",

@@ -89,6 +89,7 @@ _SIGS = {
     "dkv_attn_comp": (C.c_int, [C.POINTER(CompCacheS), DimsS, C.c_int, C.c_int, vp, vp, vp, C.c_int, vp,
                                 C.c_size_t, vp]),
     "dkv_attn_work_bytes": (C.c_size_t, [DimsS, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "dkv_pack_weight_bytes": (C.c_size_t, [C.c_int, C.c_int]),
     "dkv_pack_weight": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
     "dkv_gemm": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(EpilogueS), vp,
                            C.c_size_t, vp]),
@@ -159,6 +160,16 @@ def call(name: str, *args) -> None:
 def ptr(t) -> int | None:
     """Device (or host) address of a torch tensor, None for None."""
     return None if t is None else t.data_ptr()
+
+
+def pack_weight(w):
+    """bf16 weight [M][K] (M a multiple of 128) -> its packed tensor-core
+    layout (dkv_pack_weight), a flat bf16 device tensor."""
+    import torch
+    M, K = w.shape
+    out = torch.empty(int(load().dkv_pack_weight_bytes(M, K)) // 2, dtype=torch.bfloat16, device=w.device)
+    call("dkv_pack_weight", w.data_ptr(), M, K, out.data_ptr(), stream_ptr())
+    return out
 
 
 def stream_ptr() -> int:

@@ -28,7 +28,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 
-from .dist import replicated_select, replicated_update
+from .dist import ControllerExchange, replicated_select, replicated_update
 from . import _lib
 from .compress import CompressedKVCache
 from .config import CompressionConfig, layer_cfgs
@@ -146,6 +146,11 @@ class DraftKVEngine:
         self.full_cache_factory = full_cache_factory
         self.gamma_max = gamma_max
         self._round = 0
+        # CUDA events around the phases of each round and around rebuilds
+        # (None: off).  calibrate.py turns this on to measure the device's
+        # own draft / verify / resync / rebuild costs.
+        self.phase_events: list | None = None
+        self.rebuild_events: list | None = None
 
     # ---------------------------------------------------------------- util
     def _gamma_max(self) -> int:
@@ -256,17 +261,19 @@ class DraftKVEngine:
         sess = self.session(prompts, max_new_tokens, temperature, context_key, exchange)
         while not sess.done:
             sess.round()
+        sess.finish()
         return sess.results()
 
     def session(self, prompts: list, max_new_tokens: int, temperature: float = 0.0,
                 context_key: str | None = None, exchange=None) -> "Session":
         """Prefills `prompts` and returns a Session whose round() runs one
         draft / verify round.  `exchange` (see draftkv.dist), when given,
-        maps this process's records to the records of every process; the
-        controller selects on the largest context over all processes and is
-        updated with every process's (accepted, context, gamma), so replicated
-        controllers stay identical.  Every process must call round() the same
-        number of times."""
+        replicates the controller's inputs over processes: a
+        ControllerExchange (batched, asynchronous) or a per-round exchange
+        function; the controller selects on the largest context over all
+        processes and is updated with every process's (accepted, context,
+        gamma), so replicated controllers stay identical.  Every process must
+        call round() the same number of times, then finish()."""
         return Session(self, [list(p) for p in prompts], max_new_tokens, temperature, context_key, exchange)
 
     # -------------------------------------------------------- device round
@@ -292,8 +299,17 @@ class DraftKVEngine:
         if advance and 0 in layers and len(layers) == self.model.n_layers:
             st.comp.seen_t.zero_()
         arr = (C.c_int32 * len(layers))(*layers)
+        ev = self._event() if self.rebuild_events is not None else None
         _lib.call("dkv_comp_rebuild", st.comp.struct(), st.full.struct(), st.comp.dims(), arr, len(layers),
                   ctx_t.data_ptr(), 1 if advance else 0, _lib.stream_ptr())
+        if ev is not None:
+            self.rebuild_events.append((len(layers), ev, self._event()))
+
+    @staticmethod
+    def _event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
 
     def _resync(self, st: _Batch) -> None:
         """comp.sync_from(full, n-1) with (pos0, rows, trunc) computed on device
@@ -307,6 +323,7 @@ class DraftKVEngine:
         m = self.model
         work = st.workspace()
         V = m.vocab_size
+        ev = [self._event()] if self.phase_events is not None else None
         for i in range(gamma):
             pos_i = st.pos_draft[i]
             torch.add(st.base_pos, i, out=pos_i)
@@ -315,6 +332,8 @@ class DraftKVEngine:
             _lib.call("dkv_sample", st.draft_logits[i].data_ptr(), st.B, V, float(temperature), self.seed,
                       st.counters[i:].data_ptr(), st.vtok.data_ptr() + 4 * (i + 1), st.VS, None, 0,
                       _lib.stream_ptr())
+        if ev is not None:
+            ev.append(self._event())
         m.forward_raw(st.full, None, st.vtok.data_ptr(), st.VS, st.base_pos, st.B, gamma + 1, st.verify_logits,
                       work, st.G + 1, st.full.capacity_tokens)
         _lib.call("dkv_accept", st.verify_logits.data_ptr(), st.draft_logits.data_ptr(), st.B, gamma, V,
@@ -322,7 +341,12 @@ class DraftKVEngine:
                   st.base_pos.data_ptr(), st.accepted.data_ptr(), st.next.data_ptr(), st.rs[0].data_ptr(),
                   st.rs[1].data_ptr(), st.rs[2].data_ptr(), st.active.data_ptr(), st.accept_work.data_ptr(),
                   st.accept_work.numel(), _lib.stream_ptr())
+        if ev is not None:
+            ev.append(self._event())
         self._resync(st)
+        if ev is not None:
+            ev.append(self._event())
+            self.phase_events.append((gamma, ev))
 
     def _collect(self, st: _Batch, gamma: int) -> list:
         """(accepted, emitted tokens) per sequence -- the only device->host read."""
@@ -356,6 +380,30 @@ class Session:
         self.plen = len(prompts[0])
         self.comp_cfg = None
         self.last = None        # (cfg, gamma, [(k, emitted)]) of the latest round
+        self.batched = isinstance(exchange, ControllerExchange)
+        if self.batched:
+            exchange.start(max(len(p) for p in prompts))
+
+    def _select(self, n: list):
+        if self.batched:
+            return self.exchange.select(self.eng.controller, self.key)
+        # every process selects on the same (largest) context
+        return replicated_select(self.eng.controller, max(n), self.key, self.exchange)
+
+    def _update(self, cfg, records: list) -> None:
+        """records: (accepted, context, gamma, next context) per active
+        sequence of this process (accepted < 0: context only)."""
+        if self.batched:
+            self.exchange.update(records)
+            return
+        replicated_update(self.eng.controller, cfg, [(k, c, g) for k, c, g, _n in records if k >= 0], self.key,
+                          self.exchange)
+
+    def finish(self) -> None:
+        """Applies every outstanding exchange batch (every process calls it
+        once, after its last round)."""
+        if self.batched:
+            self.exchange.finish(self.eng.controller, self.key)
 
     @property
     def done(self) -> bool:
@@ -372,11 +420,11 @@ class Session:
         left = [self.max_new - (len(self.toks[b]) - self.plen) for b in range(B)]
         active = [lft > 0 for lft in left]
         n = [len(self.toks[b]) for b in range(B)]
-        # every process selects on the same (largest) context: replicated
-        # controllers stay identical
-        cfg, gamma = replicated_select(eng.controller, max(n), self.key, self.exchange)
+        # every process selects on the same context: replicated controllers
+        # stay identical
+        cfg, gamma = self._select(n)
         if not any(active):
-            replicated_update(eng.controller, cfg, [], self.key, self.exchange)
+            self._update(cfg, [])
             return []
         gamma = min(gamma, max(min(l for l, a in zip(left, active) if a) - 1, 0), st.G)
         st.active.copy_(torch.tensor([1 if a else 0 for a in active], dtype=torch.int32), non_blocking=True)
@@ -392,7 +440,7 @@ class Session:
                     self.res[b].verify_passes += 1
                     self.res[b].rounds.append(RoundLog(cfg, 0, 0, 1, n[b]))
             # every process takes part in every round's exchange
-            replicated_update(eng.controller, cfg, [], self.key, self.exchange)
+            self._update(cfg, [(-1, n[b], 0, n[b] + 1) for b in range(B) if active[b]])
             self.last = (cfg, 0, out)
             return out
         # drafter cache: create, or rebuild only the layers whose config changed
@@ -427,10 +475,10 @@ class Session:
             self.toks[b].extend(emitted)
             st.full.set_length(b, n[b] - 1 + gamma + 1)
             st.full.truncate_seq(b, n[b] + k)        # rollback (engine.py:216)
-            stats.append((k, n[b], gamma))
+            stats.append((k, n[b], gamma, n[b] + len(emitted)))
             self.res[b].draft_steps += gamma
             self.res[b].verify_passes += 1
             self.res[b].rounds.append(RoundLog(cfg, gamma, k, len(emitted), n[b]))
-        replicated_update(eng.controller, cfg, stats, self.key, self.exchange)
+        self._update(cfg, stats)
         self.last = (cfg, gamma, out)
         return out

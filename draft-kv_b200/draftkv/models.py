@@ -75,9 +75,7 @@ class DeviceDecoder:
             w = torch.cat([w, torch.zeros((Mp - M, K), dtype=w.dtype, device=w.device)], 0)
         if self.dtype == _lib.F32:
             return w.contiguous()
-        out = torch.empty_like(w)
-        _lib.call("dkv_pack_weight", w.data_ptr(), Mp, K, out.data_ptr(), _lib.stream_ptr())
-        return out
+        return _lib.pack_weight(w.contiguous())
 
     def _pad_bias(self, b, M):
         if b is None:
@@ -287,7 +285,7 @@ class LlamaLike(DeviceDecoder):
         head_src = w.get("lm_head.weight")
         tok_emb = self._t(emb)
         head = self._matrix(emb if head_src is None else head_src)
-        self.vocab_pad = head.shape[0] if self.dtype == _lib.F32 else _round_up(self.vocab_size, 128)
+        self.vocab_pad = _round_up(self.vocab_size, 128)     # head rows (padded to whole row tiles)
         self._rope_tables(int(self.cfg.get("max_position_embeddings", 0) or 4096))
         self._finish_struct(tok_emb, None, head, self._f32(w["model.norm.weight"]), None, layers)
 
@@ -334,7 +332,7 @@ class GPT2(DeviceDecoder):
         wte = w[f"{P}wte.weight"]
         tok_emb = self._t(wte)
         head = self._matrix(wte)
-        self.vocab_pad = head.shape[0]
+        self.vocab_pad = _round_up(self.vocab_size, 128)     # head rows (padded to whole row tiles)
         pos_emb = self._t(w[f"{P}wpe.weight"])
         self._finish_struct(tok_emb, pos_emb, head, self._f32(w[f"{P}ln_f.weight"]), self._f32(w[f"{P}ln_f.bias"]),
                             layers)

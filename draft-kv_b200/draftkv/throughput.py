@@ -62,6 +62,12 @@ class CostModel:
     fixed_verify: float = 1.0e-5
     resync_per_token: float = 2.0e-6
     controller_overhead: float = 1.0e-6
+    # Seconds to re-derive one context position of every layer of the
+    # drafter cache on a configuration switch.  None: resync_per_token, as
+    # in the reference; a cost model calibrated on the device (calibrate.py)
+    # sets it from a timed partial rebuild, since the device's per-round
+    # resync and its bulk rebuild run at very different rates per position.
+    rebuild_per_token: float | None = None
 
     def __post_init__(self) -> None:
         if self.full_kv_bandwidth is None:
@@ -110,7 +116,8 @@ class CostModel:
     def rebuild_cost(self, ctx: int, layers_changed: int | None = None) -> float:
         nl = max(1, self.n_layers)
         frac = 1.0 if layers_changed is None else min(1.0, layers_changed / nl)
-        return ctx * self.resync_per_token * frac * self.n_layers / nl
+        rate = self.resync_per_token if self.rebuild_per_token is None else self.rebuild_per_token
+        return ctx * rate * frac * self.n_layers / nl
 
     # -------------------------------------------------------- objectives
     def round_cost(self, cfg, gamma: int, alpha: float, ctx: int, extra_cost: float = 0.0) -> float:

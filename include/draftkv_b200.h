@@ -224,8 +224,9 @@ DKV_API size_t dkv_attn_work_bytes(dkv_dims dims, int group, int T, int max_ctx,
 
 /* ------------------------------------------------------------ GEMM
  * Y = X W^T for the projections, MLP and head (draftkv/llama.py:187-225,
- * draftkv/gpt2.py:191-213).  Weights are stored once in a tiled layout
- * (dkv_pack_weight) so each warp streams 512 contiguous bytes per k-step. */
+ * draftkv/gpt2.py:191-213).  bf16 runs on the tensor cores (tcgen05.mma,
+ * accumulators in tensor memory) from weights packed once by
+ * dkv_pack_weight; f32 runs on the CUDA cores from row-major weights. */
 enum {
     DKV_EPI_STORE = 0,     /* out_f32[n][m] = acc + bias                          */
     DKV_EPI_RESADD = 1,    /* h[n][m] += acc + bias                               */
@@ -251,15 +252,20 @@ typedef struct {
     int layer, n_layers;
 } dkv_epilogue;
 
-/* Tiled weight layout of W [M][K] (bf16, M % 128 == 0 after padding,
- * K % 16 == 0): [M/16][K/16][32 lanes][8] holding the mma.m16n8k16 A
- * fragments.  f32 weights are used as-is ([M][K] row-major). */
-DKV_API int dkv_pack_weight(const uint16_t* d_w, int M, int K, uint16_t* d_tiled, void* stream);
+/* Packed layout of a bf16 weight W [M][K] (M % 128 == 0 after padding,
+ * K % 16 == 0): [M/128][Kp/64][128 rows][64 k], Kp = K rounded up to 64
+ * (zero columns), each 128 x 64 block (16 KB) in the tensor core's K-major
+ * 128-byte-swizzle arrangement: row r at byte (r/8)*1024 + (r%8)*128, its
+ * 16-byte chunk c (k = 8c .. 8c+7) at chunk position c ^ (r%8).
+ * dkv_pack_weight_bytes(M, K) = M * Kp * 2.  f32 weights are used as-is
+ * ([M][K] row-major).  X (bf16) must be 16-byte aligned. */
+DKV_API size_t dkv_pack_weight_bytes(int M, int K);
+DKV_API int dkv_pack_weight(const uint16_t* d_w, int M, int K, uint16_t* d_packed, void* stream);
 
-/* The work buffer (dkv_gemm_work_bytes) must be zero when first used: the
- * split-K arrival tickets live in it and every call leaves them zero again.
- * One buffer must not serve calls that may run at the same time (different
- * streams without ordering). */
+/* The work buffer (dkv_gemm_work_bytes; a few bytes for bf16) must be zero
+ * when first used: the fp32 kernel's split-K arrival tickets live in it and
+ * every call leaves them zero again.  One buffer must not serve calls that
+ * may run at the same time (different streams without ordering). */
 DKV_API int dkv_gemm(const void* d_x, int x_dtype, const void* d_w, int w_dtype, int M, int N, int K,
              const dkv_epilogue* epi, void* d_work, size_t work_bytes, void* stream);
 DKV_API size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype);
@@ -267,16 +273,16 @@ DKV_API size_t dkv_gemm_work_bytes(int M, int N, int K, int w_dtype);
 /* dkv_gemm for callers that cannot allocate device memory: no counterpart in
  * the reference (which has no native code).  Same arguments as dkv_gemm minus
  * the work buffer, and bit-identical results (the same K split, partials
- * summed in the same order); the split-K scratch is a fixed array of
- * DKV_GEMM_NOALLOC_SCRATCH_BYTES compiled into the library, held on every GPU
- * that loads it until the process exits.  Split shapes whose scratch exceeds
- * it return DKV_EINVAL with a message (e.g. 4096 x 4096 at 320 tokens; every
- * weight of an 8B-class model fits at up to 64 tokens); unsplit shapes use
- * no scratch and have no such limit.  Allocates nothing.  The first call on
- * a device does that device's set-up (the array's device address, kernel
- * attributes); make it outside stream capture, and do not call across a
- * cudaDeviceReset() of a device already used.  All calls on a device share
- * the array: calls that overlap on the GPU race. */
+ * summed in the same order).  The bf16 kernel needs no scratch; the f32
+ * kernel's split-K scratch is a fixed array of DKV_GEMM_NOALLOC_SCRATCH_BYTES
+ * compiled into the library, held on every GPU that loads it until the
+ * process exits.  f32 split shapes whose scratch exceeds it return DKV_EINVAL
+ * with a message (e.g. 4096 x 4096 at 320 tokens); unsplit shapes use no
+ * scratch and have no such limit.  Allocates nothing.  The first f32 call on
+ * a device does that device's set-up (the array's device address); make it
+ * outside stream capture, and do not call across a cudaDeviceReset() of a
+ * device already used.  All calls on a device share the array: calls that
+ * overlap on the GPU race. */
 #define DKV_GEMM_NOALLOC_SCRATCH_BYTES (16u << 20)
 DKV_API int dkv_gemm_noalloc(const void* d_x, int x_dtype, const void* d_w, int w_dtype, int M, int N, int K,
                              const dkv_epilogue* epi, void* stream);

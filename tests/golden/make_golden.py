@@ -69,9 +69,14 @@ def small_model_weights(W, name):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
+    ap.add_argument("--only", choices=["adaptive"], default=None,
+                    help="write only this fixture (the others are left as they are)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     import draftkv as ref                          # the reference package
+    if args.only == "adaptive":
+        adaptive_fixtures(ref)
+        return
     from draftkv import compress as rc
     from draftkv.gpt2 import GPT2
     from draftkv.llama import LlamaLike
@@ -235,7 +240,89 @@ def main():
         ptrace.append(dict(t=t, cut=cut, n=n, tables=[list(map(int, pk.block_table[L])) for L in range(2)],
                            free=list(map(int, pk.pool._free)), frag=pk.fragmentation()))
     (HERE / "paged_trace.json").write_text(json.dumps(ptrace))
+    adaptive_fixtures(ref)
     print("golden fixtures written to", HERE)
+
+
+# ---------------------------------------------------------------- adaptive allocator
+ADAPTIVE_NL = 6
+ADAPTIVE_CTX = 32768
+
+
+def adaptive_setup(ref_or_ours, resync=1.0e-7):
+    """Candidates, cost model and budget function of the adaptive-allocator
+    scenarios (the shapes of the reference's tests/test_adaptive.py:15-35),
+    built from either package's CompressionConfig / CostModel / LayerPlan."""
+    m = ref_or_ours
+    cands = [m.CompressionConfig(4, 0.25), m.CompressionConfig(4, 0.5), m.CompressionConfig(4, 1.0)]
+    cm = m.CostModel(n_layers=ADAPTIVE_NL, n_kv_heads=12, d_head=64, weight_bytes=2.0e9,
+                     full_kv_bandwidth=6.4e10, hbm_kv_budget=4.0e8, resync_per_token=resync)
+    lo = m.LayerPlan.uniform(cands[0], ADAPTIVE_NL).per_layer_bytes(ADAPTIVE_CTX, 12, 64)
+    hi = m.LayerPlan.uniform(cands[-1], ADAPTIVE_NL).per_layer_bytes(ADAPTIVE_CTX, 12, 64)
+    return cands, cm, (lambda frac: lo + frac * (hi - lo))
+
+
+# (name, controller kwargs, phases of (env damage, env seed, rounds, key)); a
+# phase with env seed None keeps the previous environment and shifts its damage
+ADAPTIVE_SCENARIOS = [
+    ("find", dict(budget=0.5, probe_prob=0.4, resolve_every=40, seed=2), [({2: 2.5}, 1, 900, None)]),
+    ("shift", dict(budget=0.5, probe_prob=0.4, resolve_every=40, decay=0.97, seed=6),
+     [({1: 2.5}, 5, 800, None), ({4: 2.5}, None, 1200, None)]),
+    ("keys", dict(budget=0.5, probe_prob=0.4, resolve_every=40, seed=7),
+     [({0: 2.5}, 8, 700, "prose"), ({5: 2.5}, 9, 700, "code")]),
+    ("rate", dict(budget=0.6, probe_prob=0.1, resolve_every=50, seed=11), [({3: 1.0}, 10, 1000, None)]),
+    ("stall", dict(budget=0.2, probe_prob=0.3, resolve_every=25, seed=13),
+     [({L: 4.0 for L in range(ADAPTIVE_NL)}, 14, 300, None)]),
+]
+
+
+def adaptive_fixtures(ref):
+    """Decision logs of the reference's AdaptiveLayerController
+    (adaptive.py:68-335) driven by its simulated per-layer environment
+    (sim.py:131-167): per round the plan (candidate index per layer), gamma
+    and the accepted count the environment returned; plus the reference's
+    exact knapsack (layers.py:301-368) on random damage tables and its probe
+    throttle."""
+    from draftkv.adaptive import AdaptiveLayerController
+    from draftkv.layers import SensitivityProfile, allocate
+    from draftkv.sim import LayerEnv
+    logs = {}
+    for name, kw, phases in ADAPTIVE_SCENARIOS:
+        cands, cm, budget = adaptive_setup(ref)
+        kw = dict(kw)
+        ctrl = AdaptiveLayerController(cm, ADAPTIVE_NL, budget(kw.pop("budget")), cands, ctx_hint=ADAPTIVE_CTX, **kw)
+        env, rounds = None, []
+        for dmg, seed, n, key in phases:
+            if seed is None:
+                env.shift(dmg)
+            else:
+                env = LayerEnv(damage=dmg, ranked=cands, ctx=ADAPTIVE_CTX, seed=seed)
+            for _ in range(n):
+                plan, g = ctrl.select(env.ctx, key)
+                k = env.pull(plan, g) if g > 0 else 0
+                ctrl.update(plan, g, k, env.ctx, key)
+                rounds.append([[cands.index(c) for c in plan], g, k])
+        logs[name] = dict(rounds=rounds, damages={str(k): ctrl.damages(k) for k in ctrl.stats},
+                          probes=ctrl.n_probes, resolves=ctrl.n_resolves, recoveries=ctrl.n_stall_recoveries)
+    rng = np.random.default_rng(31)
+    knap = []
+    cands, cm, budget = adaptive_setup(ref)
+    for t in range(12):
+        prof = SensitivityProfile(cands[-1], 0.9, tuple(cands))
+        for L in range(ADAPTIVE_NL):
+            for c in cands[:-1]:
+                prof.alpha[(L, c)] = float(0.9 * np.exp(-rng.uniform(0.0, 3.0)))
+        frac = float(rng.uniform(-0.1, 1.1))
+        plan = allocate(prof, budget(frac), ADAPTIVE_CTX, 12, 64, ADAPTIVE_NL)
+        knap.append(dict(alpha=[[L, cands.index(c), a] for (L, c), a in prof.alpha.items()], frac=frac,
+                         plan=[cands.index(c) for c in plan]))
+    probe = {}
+    for resync in (1.0e-8, 2.0e-6):
+        cands, cm, budget = adaptive_setup(ref, resync)
+        ctrl = AdaptiveLayerController(cm, ADAPTIVE_NL, budget(0.6), cands, ctx_hint=ADAPTIVE_CTX, probe_prob=0.3,
+                                       seed=1)
+        probe[str(resync)] = [ctrl.effective_probe_prob(c) for c in (256, 4096, ADAPTIVE_CTX)]
+    (HERE / "adaptive.json").write_text(json.dumps(dict(logs=logs, knapsack=knap, probe=probe)))
 
 
 if __name__ == "__main__":

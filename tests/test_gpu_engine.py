@@ -231,3 +231,66 @@ def test_host_resident_full_cache_is_identical(golden, dtype):
     base = DraftKVEngine(m, seed=0)
     base.offload_full = True
     assert base.generate_baseline(prompt, 24, 0.0) == dev.tokens
+
+
+# ---------------------------------------------------------------- per-layer plans
+def _four_layer_llama():
+    from draftkv import from_config
+    cfg = W.llama_config(4, 128, 4, 2, 192, 101, head_dim=64, tied=True, dtype="f32")
+    return from_config(W.make_weights(cfg, seed=5, std=0.09, attn_gain=3.0, attn_sharpness=3.0), cfg)
+
+
+def test_adaptive_layer_plans_are_lossless_and_rebuild_only_changed_layers():
+    """Reference tests/test_adaptive.py:130-171 on the device.  The adaptive
+    allocator probes swaps on almost every round (probe_prob 0.9) and
+    re-solves its plan every 5 decisions; the greedy stream must equal plain
+    full-KV decoding, and every plan change must rebuild exactly the layers
+    whose configuration changed."""
+    from draftkv import AdaptiveLayerController, DraftKVEngine, LayerPlan
+    m = _four_layer_llama()
+    prompt = W.tokens(192, m.vocab_size, seed=3)
+    base = DraftKVEngine(m, seed=0).generate_baseline(prompt, 32, 0.0)
+    cands = [CompressionConfig(4, 0.25), CompressionConfig(4, 0.5), CompressionConfig(4, 1.0)]
+    cm = CostModel(n_layers=m.n_layers, n_kv_heads=m.n_kv_heads, d_head=m.d_head, weight_bytes=2.0e6,
+                   bandwidth=2.0e10, full_kv_bandwidth=6.4e8, hbm_kv_budget=2.0e5)
+    lo = LayerPlan.uniform(cands[0], m.n_layers).per_layer_bytes(256, m.n_kv_heads, m.d_head)
+    hi = LayerPlan.uniform(cands[-1], m.n_layers).per_layer_bytes(256, m.n_kv_heads, m.d_head)
+    ctrl = AdaptiveLayerController(cm, m.n_layers, lo + 0.5 * (hi - lo), cands, ctx_hint=256, probe_prob=0.9,
+                                   resolve_every=5, seed=3)
+    eng = DraftKVEngine(m, ctrl, seed=0)
+    calls, plans = [], []
+    real = eng._rebuild
+
+    def spy(st, layers, ctx_t, advance):
+        calls.append(list(layers))
+        plans.append(list(st.comp.cfgs))
+        real(st, layers, ctx_t, advance)
+
+    eng._rebuild = spy
+    r = eng.generate(prompt, 32, 0.0)
+    assert r.tokens == base
+    assert ctrl.n_probes > 0 and r.cache_rebuilds >= 3
+    assert calls[0] == list(range(m.n_layers))          # first sync: every layer
+    for prev, cur, layers in zip(plans, plans[1:], calls[1:]):
+        assert layers and layers == [L for L in range(m.n_layers) if prev[L] != cur[L]]
+
+
+def test_partial_rebuild_leaves_other_layers_untouched():
+    """Reference tests/test_adaptive.py:130-150: rebuilding one layer for a
+    new configuration rewrites that layer only (device cache, read back)."""
+    from draftkv import CompressedKVCache, FullKVCache
+    m = _four_layer_llama()
+    toks = np.arange(64) % m.vocab_size
+    full = FullKVCache(m.n_layers)
+    m.forward(toks, full, 0)
+    comp = CompressedKVCache(m.n_layers, CompressionConfig(4, 1.0))
+    comp.materialize(m.n_kv_heads, m.d_head, m.dtype)
+    comp.sync_from(full, 0)
+    before = [comp.read(L)[0].copy() for L in range(m.n_layers)]
+    cfgs = [CompressionConfig(4, 1.0)] * m.n_layers
+    cfgs[1] = CompressionConfig(4, 0.25)
+    rows = comp.rebuild_layers(full, [1], cfgs)
+    assert rows == 64
+    assert comp.cfgs[1] == CompressionConfig(4, 0.25)
+    for L in range(m.n_layers):
+        assert np.array_equal(comp.read(L)[0], before[L]) == (L != 1), L

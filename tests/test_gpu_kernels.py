@@ -248,8 +248,7 @@ def test_bf16_gemm_matches_torch_and_is_batch_invariant(M, K):
     L = lib()
     g = torch.Generator(device="cuda").manual_seed(M + K)
     W = (torch.randn((M, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
-    Wt = torch.empty_like(W)
-    L.call("dkv_pack_weight", W.data_ptr(), M, K, Wt.data_ptr(), L.stream_ptr())
+    Wt = L.pack_weight(W)
     X = torch.randn((100, K), generator=g, device="cuda").to(torch.bfloat16)
     ref = X.float() @ W.float().t()
     outs = {}

@@ -31,9 +31,12 @@ emitted is compared with it ("lossless", greedy output must be identical),
 and its rounds at the positions of the timed region give the full-KV
 baseline the speedup is measured against.
 
-Multi-GPU (torchrun): sequences shard by rank (weak scaling, 4 per GPU); the
-only collective is a per-round all-gather of (accepted, context) per sequence
-that keeps the replicated controllers identical.
+Multi-GPU (torchrun): sequences shard by rank (weak scaling, 4 per GPU);
+the only collectives are the controller's inputs -- (accepted, context,
+gamma) per sequence, gathered every 8 rounds by an asynchronous all-gather
+and applied 2 rounds later on every rank, which keeps the replicated
+controllers identical without holding the ranks in step every round -- and
+one gather of the emitted token ids at the end.
 
 The JSON line reports emitted tokens/s (value: device-timed rounds; e2e: wall
 clock through the public engine API with its per-round host<->device copies),
@@ -396,8 +399,10 @@ def run_gpu(args) -> None:
 
     exchange = None
     if world > 1:
-        from draftkv.dist import allgather_exchange
-        exchange = allgather_exchange(B, device="cuda")
+        # the controller's inputs cross ranks in batches of 8 rounds, applied
+        # 2 rounds after they ship (asynchronous NCCL all-gather)
+        from draftkv.dist import ControllerExchange
+        exchange = ControllerExchange(B, period=8, lag=2, device="cuda")
 
     engine = DraftKVEngine(model, ctrl, seed=rank, gamma_max=G)
     engine.offload_full = bool(conf.get("offload"))
@@ -417,22 +422,24 @@ def run_gpu(args) -> None:
         from draftkv.calibrate import calibrate_cost_model
         cm_cal, calib = calibrate_cost_model(sess, cm, CompressionConfig(8, 1.0), 2)
         if world > 1:
-            v = torch.tensor([cm_cal.fixed_draft, cm_cal.fixed_verify, cm_cal.resync_per_token,
-                              cm_cal.rebuild_per_token or 0.0], dtype=torch.float64, device="cuda")
+            v = torch.tensor([cm_cal.bandwidth, cm_cal.full_kv_bandwidth, cm_cal.fixed_draft, cm_cal.fixed_verify,
+                              cm_cal.resync_per_token, cm_cal.rebuild_per_token or 0.0], dtype=torch.float64,
+                             device="cuda")
             dist.all_reduce(v, op=dist.ReduceOp.SUM)
             v = (v / world).tolist()
             from dataclasses import replace
-            cm_cal = replace(cm_cal, fixed_draft=v[0], fixed_verify=v[1], resync_per_token=v[2],
-                             rebuild_per_token=v[3] or None)
+            cm_cal = replace(cm_cal, bandwidth=v[0], full_kv_bandwidth=v[1], fixed_draft=v[2], fixed_verify=v[3],
+                             resync_per_token=v[4], rebuild_per_token=v[5] or None)
         arms = [CompressionConfig(b, k) for b, k in conf["arms"]] if "arms" in conf else default_arms()
         ctrl = ThompsonController(cm_cal, arms, gamma_max=G, seed=0)
         engine.controller = ctrl
         calib = {k: (round(v, 9) if isinstance(v, float) else v) for k, v in calib.items()}
-        calib.update({"used": {"fixed_draft": cm_cal.fixed_draft, "fixed_verify": cm_cal.fixed_verify,
+        calib.update({"used": {"bandwidth": cm_cal.bandwidth, "full_kv_bandwidth": cm_cal.full_kv_bandwidth,
+                               "fixed_draft": cm_cal.fixed_draft, "fixed_verify": cm_cal.fixed_verify,
                                "resync_per_token": cm_cal.resync_per_token,
                                "rebuild_per_token": cm_cal.rebuild_per_token},
-                      "defaults": {"fixed_draft": cm.fixed_draft, "fixed_verify": cm.fixed_verify,
-                                   "resync_per_token": cm.resync_per_token},
+                      "defaults": {"bandwidth": cm.bandwidth, "fixed_draft": cm.fixed_draft,
+                                   "fixed_verify": cm.fixed_verify, "resync_per_token": cm.resync_per_token},
                       "ceiling_4b_keep0.25": round(cm_cal.ceiling(CompressionConfig(4, 0.25), ctx), 4)})
     explore = None
     if settle:
@@ -513,8 +520,13 @@ def run_gpu(args) -> None:
         _lib.check(lib.dkv_prof_summary(i, C.byref(ms), C.byref(n), C.byref(by)), "dkv_prof_summary")
         prof[nm] = dict(ms=ms.value, launches=n.value, bytes=by.value)
     prof_launches = sum(v["launches"] for v in prof.values())
+    sess.finish()
     spec_streams = [list(t) for t in sess.toks]
     plen = len(prompts[0])
+    gathered = None
+    if world > 1:
+        from draftkv.dist import gather_tokens
+        gathered = sum(len(t) - plen for t in gather_tokens(spec_streams))
     del sess
     model._graphs.clear()
     torch.cuda.empty_cache()
@@ -536,7 +548,8 @@ def run_gpu(args) -> None:
     b_len = min(b_len, n_check - b_start)
     beng = DraftKVEngine(model, FixedPolicy(CompressionConfig(16, 1.0), 0), seed=rank, gamma_max=G)
     beng.offload_full = bool(conf.get("offload"))
-    bsess = beng.session(prompts, n_check, T, exchange=exchange)
+    # a fixed policy needs no replication: ranks decode independently
+    bsess = beng.session(prompts, n_check, T)
     for _ in range(b_start):
         bsess.round()
     btoks, bdev_s, bwall_s, _, _, _, _ = timed_rounds(bsess, b_len, profile=False)
@@ -634,6 +647,9 @@ def run_gpu(args) -> None:
                    **({"h2d_gbs": round(h2d_bw / 1e9, 1)} if h2d_bw else {})},
         "lossless": lossless,
         "lossless_tokens_compared": compared,
+        "tokens_gathered": gathered,
+        "exchange": (f"batched async all-gather: every {exchange.period} rounds, applied {exchange.lag} rounds later, "
+                     f"{exchange.batches} batches" if exchange is not None else None),
         "cost_model_calibration": calib,
         "controller_settle_rounds": settle,
         "explore": ({"rounds": explore["rounds"], "tokens_per_s": explore["tokens_per_s"],
@@ -813,6 +829,17 @@ def run_kernel(args) -> None:
         full = FullKVCache(1, n_kv, d, "bf16", capacity=ctx + 64, batch=B)
         for b in range(B):
             full.ensure(b, ctx + 16)
+        if not args.no_shuffle:
+            # configuration 2: the page table shuffled from a seed (pages of a
+            # sequence scattered over the pool)
+            used = sorted({blk for b in range(B) for blk in full.block_tables[b][0]})
+            perm = dict(zip(used, np.random.default_rng(7).permutation(used).tolist()))
+            for b in range(B):
+                tbl = full.block_tables[b][0]
+                for i, blk in enumerate(tbl):
+                    tbl[i] = perm[blk]
+                    full.table_host[b, 0, i] = perm[blk]
+            full._dirty = True
         g = torch.Generator(device="cuda").manual_seed(0)
         # K/V ~ N(0, 1) with 1% of the channels (seeded) scaled x8 as outliers
         ch = torch.randperm(d, generator=torch.Generator().manual_seed(1))[: max(1, d // 100)].to("cuda")
@@ -856,7 +883,8 @@ def run_kernel(args) -> None:
         us = timeit(lambda: _lib.call("dkv_attn_full", full.struct(), full.dims(), 0, G, T, qv.data_ptr(),
                                       p0.data_ptr(), outv.data_ptr(), _lib.BF16, args.split, work.data_ptr(), work.numel(),
                                       _lib.stream_ptr()))
-        line["config"] = {"batch": B, "ctx": ctx, "T": T, "n_kv": n_kv, "d_head": d, "group": G, "split": args.split}
+        line["config"] = {"batch": B, "ctx": ctx, "T": T, "n_kv": n_kv, "d_head": d, "group": G, "split": args.split,
+                          "pages": "sequential" if args.no_shuffle else "shuffled (seed 7)"}
     else:
         M, K, N = args.M, args.K, args.N
         g = torch.Generator(device="cuda").manual_seed(0)
@@ -914,6 +942,7 @@ def main() -> None:
     ap.add_argument("--N", type=int, default=4)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--split", type=int, default=512, help="keys per split (verify-attn)")
+    ap.add_argument("--no-shuffle", action="store_true", help="kernel mode: keep the page table in allocation order")
     args = ap.parse_args()
     if args.kernel:
         run_kernel(args)

@@ -225,6 +225,7 @@ KeySrc full_src(const dkv_full_cache* f) {
     for (int sh = 0; sh < 31; ++sh)
         if ((1 << sh) == f->page_size) k.page_shift = sh;
     k.max_pages = f->max_pages;
+    k.n_pages = f->n_pages;
     k.dtype = f->dtype;
     k.comp = false;
     return k;
@@ -254,7 +255,9 @@ using namespace dkv;
 constexpr size_t kAttnTickets = 16384;
 
 static size_t attn_scratch(int batch, int n_kv, int n_splits, int R, int d, int cap, int group, bool comp) {
-    const int n_rb = (R + kGenRB - 1) / kGenRB;
+    // row blocks: up to 64 rows the tensor-core kernel takes 16 rows a CTA
+    // (each block keeps a 64-row partial stride), beyond that 64 a CTA
+    const int n_rb = comp ? (R + kGenRB - 1) / kGenRB : (R <= kGenRB ? (R + 15) / 16 : (R + kGenRB - 1) / kGenRB);
     size_t b = kAttnTickets * sizeof(unsigned);
     b += align_up((size_t)batch * n_kv * n_rb * n_splits * kGenRB * (d + 2) * sizeof(float), 256);
     if (comp) b += align_up((size_t)batch * n_kv * group * cap * sizeof(float), 256);

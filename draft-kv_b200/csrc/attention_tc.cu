@@ -2,17 +2,27 @@
 // decode and prefill chunks.  Replaces draftkv/llama.py:202-219 /
 // draftkv/gpt2.py:197-207 over FullKVCache / PagedKVCache.
 //
-// One CTA per (key split, KV head, sequence x row block); 4 warps.  K/V pages
-// of the split stream through a double-buffered, XOR-swizzled shared-memory
-// tile of 64 keys with cp.async; warp w owns query rows [16w, 16w+16) of the
-// CTA (rows = token x GQA head) and runs S = Q K^T and O += P V with
-// mma.sync.m16n8k16 (bf16 in, fp32 accumulate) and a per-row online softmax.
+// Prefill chunks (> 64 query rows): one CTA per (key split, KV head, sequence
+// x row block); 4 warps.  K/V pages of the split stream through a
+// double-buffered, XOR-swizzled shared-memory tile of 64 keys with cp.async;
+// warp w owns query rows [16w, 16w+16) of the CTA (rows = token x GQA head)
+// and runs S = Q K^T and O += P V with mma.sync.m16n8k16 (bf16 in, fp32
+// accumulate) and a per-row online softmax.  Decode and verify (<= 64 rows)
+// take attn_kq_kernel below, whose tiles the copy engine (TMA) fetches one
+// page at a time when the pool is in device memory.
 // The CTA partials merge in split order (split_merge), so a row's result does
 // not depend on how many rows share the launch: verify row i equals the
 // one-token decode at that position bit for bit.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "attn_common.cuh"
 
 namespace dkv {
+
+uint32_t* device_error_word();
 
 DKV_DEV uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -273,14 +283,26 @@ __global__ void __launch_bounds__(kTcThreads) attn_full_tc_kernel(AttnArgs a) {
 // the launch: verify rows equal decode rows bit for bit.  Scores are kept in
 // log2 units (log2 e folded into the query scale); partials store the max in
 // natural units for the split merge.
+//
+// Tiles come through a 3-deep ring of 64-key slots.  With the pool in device
+// memory (TMA = true) thread 0 fetches a tile with one 4-D tensor copy per
+// (page, K or V, 64 dims) -- 16 copies of 2 KB for d = 128 -- completing on
+// the slot's mbarrier, in the copy engine's 128-byte swizzle; keys past the
+// split's end get zero V rows.  With the pool in pinned host memory
+// (configuration 5) every thread issues 16-byte cp.async copies.
 constexpr int kKqKG = 4;
 constexpr int kKqNST = 3;
+// Query rows per CTA: at most 2 row tiles (8 warps, no register spills, two
+// CTAs per SM); more rows (a verify of gamma + 1 tokens x the GQA group) take
+// more CTAs per (split, head), whose tiles the later ones mostly find in L2.
+// A row's arithmetic is the same in any CTA.
+constexpr int kKqRows = 16;
 
 template <int D>
 size_t kq_smem(int RT) {
     const size_t ring = (size_t)kKqNST * 2 * kTcKT * D * 2;
     const size_t merge = (size_t)RT * kKqKG * 8 * (D + 2) * sizeof(float);
-    return ring > merge ? ring : merge;
+    return (ring > merge ? ring : merge) + 1024;      // + alignment slack
 }
 
 DKV_DEV uint32_t movm_trans(uint32_t x) {
@@ -289,21 +311,58 @@ DKV_DEV uint32_t movm_trans(uint32_t x) {
     return y;
 }
 
-template <int D, int MAXT>
-__global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
+// Tensor maps of the K and V pools for the TMA-fed kernel: 4-D views
+// {d, 16 page rows, n_kv, n_pages} with a box of {64, 16, 1, 1} (one page's
+// 16 keys of one head, 64 dims) and 128-byte swizzle.
+struct KvMaps {
+    CUtensorMap k, v;
+};
+
+// Element offset of (key, 16-byte chunk) in a 64-key K or V tile.  TMA
+// tiles: [d/64 halves][64 keys][64 dims], 128-byte rows with the chunk XOR
+// (key % 8) that the copy engine's swizzle writes; cp.async tiles: [64][d]
+// with the same XOR on the low chunk bits (both conflict-free for ldmatrix).
+template <int D, bool TMA>
+DKV_DEV int kv_off(int key, int chunk) {
+    if constexpr (TMA)
+        return (chunk >> 3) * (kTcKT * 64) + key * 64 + (((chunk & 7) ^ (key & 7)) << 3);
+    else
+        return swz<D>(key, chunk);
+}
+
+DKV_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];\n" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <int D, int MAXT, bool TMA>
+__global__ void __launch_bounds__(MAXT, 2) attn_kq_kernel(const __grid_constant__ KvMaps maps, AttnArgs a) {
     constexpr int DC = D / 8;      // 16-byte chunks per key row
     constexpr int KS = D / 16;     // k16 steps over d
     constexpr int PS = D + 2;
     constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
-    extern __shared__ __align__(128) uint8_t tsm[];
+    extern __shared__ __align__(128) uint8_t tsm_raw[];
+    // 1024-byte aligned base (the 128-byte swizzle of the copy engine)
+    uint8_t* tsm = tsm_raw + ((1024u - (smem_u32(tsm_raw) & 1023u)) & 1023u);
     __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(tsm);      // [NST][K 64xD | V 64xD]
     __shared__ float ms[kAttnRB], ls[kAttnRB];
+    __shared__ __align__(8) uint64_t full_bar[kKqNST];
+    if (TMA && threadIdx.x == 0) {
+        for (int i = 0; i < kKqNST; ++i) mbar_init(&full_bar[i], 1);
+        fence_async_shared();
+    }
+    if (TMA) __syncthreads();    // the barriers are initialised before anyone waits on them
     pdl_trigger();
     pdl_wait();         // queries and the new cache rows come from the previous kernel
 
-    const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int s = blockIdx.x, h = blockIdx.y;
+    const int b = blockIdx.z / a.n_rb, rb = blockIdx.z % a.n_rb;
     const int G = a.group, T = a.T;
-    const int R = T * G;
+    const int rbase = rb * kKqRows;                 // this CTA's rows: rbase .. rbase + R - 1
+    const int R = min(kKqRows, T * G - rbase);
     const int nthreads = blockDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kg = warp % kKqKG, rt = warp / kKqKG;
@@ -324,7 +383,8 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
     uint32_t qb[KS][2];
     {
         const int r = rt * 8 + qr;
-        const float* qv = r < R ? a.q + (((size_t)b * T + r / G) * HQ + h * G + r % G) * D : nullptr;
+        const int gr = rbase + r;                   // row of the launch
+        const float* qv = r < R ? a.q + (((size_t)b * T + gr / G) * HQ + h * G + gr % G) * D : nullptr;
         const float sc = a.scale * kLog2e;
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
@@ -334,7 +394,7 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
         }
     }
     // this thread's S columns: rows 8rt + 2qc (0) and 8rt + 2qc + 1 (1)
-    const int r0 = rt * 8 + 2 * qc;
+    const int r0 = rbase + rt * 8 + 2 * qc;
     const int qp0 = qbase + r0 / G, qp1 = qbase + (r0 + 1) / G;
 
     float m0 = -INFINITY, m1 = -INFINITY;
@@ -349,39 +409,74 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
     auto load_tile = [&](int slot, int t0) {
         __nv_bfloat16* kd = ring + (size_t)slot * 2 * kTcKT * D;
         __nv_bfloat16* vd = kd + kTcKT * D;
-#pragma unroll 4
-        for (int i = threadIdx.x; i < kTcKT * DC; i += nthreads) {
-            const int key = i / DC, ch = i % DC;
-            const int kp = t0 + key;
-            const bool ok = kp < k1;
-            size_t off = 0;
-            if (ok) {
-                const int page = __ldg(ptab + (kp >> psh));
-                off = ((((size_t)page * a.n_kv + h) << psh) + (kp & pmask)) * D + ch * 8;
+        if constexpr (TMA) {
+            // one thread: per 16-key page with a live key, D/64 boxes of K
+            // and of V; pages wholly past the split's last key are skipped
+            if (threadIdx.x == 0) {
+                const int np = min(kTcKT / 16, (k1 - t0 + 15) / 16);
+                mbar_expect_tx(&full_bar[slot], (uint32_t)np * 2 * (D / 64) * (16 * 64 * 2));
+                for (int j = 0; j < np; ++j) {
+                    const int page = __ldg(ptab + ((t0 >> 4) + j));
+#pragma unroll
+                    for (int x = 0; x < D / 64; ++x) {
+                        tma_load_4d(kd + x * (kTcKT * 64) + j * 16 * 64, &maps.k, x * 64, 0, h, page, &full_bar[slot]);
+                        tma_load_4d(vd + x * (kTcKT * 64) + j * 16 * 64, &maps.v, x * 64, 0, h, page, &full_bar[slot]);
+                    }
+                }
             }
-            cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
-            cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
+        } else {
+#pragma unroll 4
+            for (int i = threadIdx.x; i < kTcKT * DC; i += nthreads) {
+                const int key = i / DC, ch = i % DC;
+                const int kp = t0 + key;
+                const bool ok = kp < k1;
+                size_t off = 0;
+                if (ok) {
+                    const int page = __ldg(ptab + (kp >> psh));
+                    off = ((((size_t)page * a.n_kv + h) << psh) + (kp & pmask)) * D + ch * 8;
+                }
+                cpasync16(kd + swz<D>(key, ch), kpool + off, ok);
+                cpasync16(vd + swz<D>(key, ch), vpool + off, ok);
+            }
         }
     };
+    bool ok_all = true;
 #pragma unroll
     for (int i = 0; i < kKqNST - 1; ++i) {
         if (i < ntiles) load_tile(i, k0 + i * kTcKT);
-        asm volatile("cp.async.commit_group;\n" ::);
+        if constexpr (!TMA) asm volatile("cp.async.commit_group;\n" ::);
     }
     for (int it = 0; it < ntiles; ++it) {
         const int t0 = k0 + it * kTcKT;
+        const int slot = it % kKqNST;
         if (it + kKqNST - 1 < ntiles) load_tile((it + kKqNST - 1) % kKqNST, t0 + (kKqNST - 1) * kTcKT);
-        asm volatile("cp.async.commit_group;\n" ::);
-        asm volatile("cp.async.wait_group %0;\n" ::"n"(kKqNST - 1));
-        __syncthreads();
-        const __nv_bfloat16* kt = ring + (size_t)(it % kKqNST) * 2 * kTcKT * D;
+        const __nv_bfloat16* kt = ring + (size_t)slot * 2 * kTcKT * D;
         const __nv_bfloat16* vt = kt + kTcKT * D;
+        if constexpr (TMA) {
+            ok_all = mbar_wait(&full_bar[slot], (uint32_t)((it / kKqNST) & 1), a.err) && ok_all;
+            if (t0 + kTcKT > k1) {
+                // keys past the split's end: the rest of the last page holds
+                // whatever the pool held there, and whole pages were not
+                // copied; their probabilities are zero, so zero their V rows
+                // (0 x NaN would not be 0)
+                __nv_bfloat16* vz = const_cast<__nv_bfloat16*>(vt);
+                for (int i = threadIdx.x; i < (t0 + kTcKT - k1) * DC; i += nthreads) {
+                    const int key = k1 - t0 + i / DC, ch = i % DC;
+                    *reinterpret_cast<uint4*>(vz + kv_off<D, true>(key, ch)) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                __syncthreads();
+            }
+        } else {
+            asm volatile("cp.async.commit_group;\n" ::);
+            asm volatile("cp.async.wait_group %0;\n" ::"n"(kKqNST - 1));
+            __syncthreads();
+        }
         // ---- S^T: rows keys 16kg + qr (+8), columns query rows
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
             uint32_t af[4];
-            ldsm4(af[0], af[1], af[2], af[3], kt + swz<D>(kg * 16 + (mi & 1) * 8 + ri, 2 * kk + (mi >> 1)));
+            ldsm4(af[0], af[1], af[2], af[3], kt + kv_off<D, TMA>(kg * 16 + (mi & 1) * 8 + ri, 2 * kk + (mi >> 1)));
             mma_bf16_16816(sc, af, qb[kk][0], qb[kk][1]);
         }
         // ---- causal / range mask
@@ -428,12 +523,21 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
 #pragma unroll
         for (int md = 0; md < KS; ++md) {
             uint32_t va[4];
-            ldsm4t(va[0], va[1], va[2], va[3], vt + swz<D>(kg * 16 + (mi >> 1) * 8 + ri, 2 * md + (mi & 1)));
+            ldsm4t(va[0], va[1], va[2], va[3], vt + kv_off<D, TMA>(kg * 16 + (mi >> 1) * 8 + ri, 2 * md + (mi & 1)));
             mma_bf16_16816(oacc[md], va, pb0, pb1);
         }
         __syncthreads();          // the ring slot is refilled next
     }
-    asm volatile("cp.async.wait_group 0;\n" ::);
+    if constexpr (TMA) {
+        if (!ok_all && threadIdx.x == 0) {
+            // a copy never completed: wait (bounded) for any still in flight
+            // before the shared memory is reused
+            for (int it = max(0, ntiles - kKqNST); it < ntiles; ++it)
+                mbar_wait(&full_bar[it % kKqNST], (uint32_t)((it / kKqNST) & 1), nullptr);
+        }
+    } else {
+        asm volatile("cp.async.wait_group 0;\n" ::);
+    }
     __syncthreads();
 
     // ---- merge the 4 key groups of each row (fixed order) into the split partial
@@ -458,7 +562,7 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
         }
     }
     __syncthreads();
-    const size_t bhr = (size_t)b * a.n_kv + h;
+    const size_t bhr = ((size_t)b * a.n_kv + h) * a.n_rb + rb;
     float* mypart = a.part + ((bhr * a.n_splits + s) * kAttnRB) * PS;
     for (int i = threadIdx.x; i < R * (D + 1); i += nthreads) {
         const int r = i / (D + 1), e = i % (D + 1);      // e == D: the row's (max, sum)
@@ -479,7 +583,7 @@ __global__ void __launch_bounds__(MAXT, 1) attn_kq_kernel(AttnArgs a) {
             mypart[(size_t)r * PS + 2 + e] = acc;
         }
     }
-    split_merge(a, bhr, b, h, R, 0, ms, ls);
+    split_merge(a, bhr, b, h, R, rbase, ms, ls);
 }
 
 template <int D>
@@ -487,11 +591,59 @@ size_t full_tc_smem() {
     return (size_t)4 * kTcKT * D * 2 + 2 * kAttnRB * sizeof(float);
 }
 
-template <int D, int MAXT>
-cudaError_t launch_kq(const AttnArgs& a, dim3 grid, int threads, cudaStream_t st) {
-    const cudaError_t e = allow_smem_max_once<attn_kq_kernel<D, MAXT>>();
+template <int D, int MAXT, bool TMA>
+cudaError_t launch_kq(const KvMaps& maps, const AttnArgs& a, dim3 grid, int threads, cudaStream_t st) {
+    const cudaError_t e = allow_smem_max_once<attn_kq_kernel<D, MAXT, TMA>>();
     if (e != cudaSuccess) return e;
-    return launch_pdl(attn_kq_kernel<D, MAXT>, grid, dim3(threads), kq_smem<D>((threads / 32) / kKqKG), st, a);
+    return launch_pdl(attn_kq_kernel<D, MAXT, TMA>, grid, dim3(threads), kq_smem<D>((threads / 32) / kKqKG), st,
+                      maps, a);
+}
+
+int encode_bf16_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                    const uint32_t* box);
+
+// Tensor maps of a device-resident pool with 16-row pages (cached per pool);
+// false when the pool is elsewhere (pinned host memory: the cp.async path).
+bool kv_maps(const KeySrc& src, int n_kv, int d, KvMaps* out) {
+    struct Entry {
+        const void* k;
+        const void* v;
+        int n_kv, d, n_pages;
+        bool ok;
+        KvMaps maps;
+    };
+    static std::mutex mu;
+    static Entry cache[32];
+    static int n = 0, next = 0;
+    if (src.page_size != 16 || (d != 64 && d != 128) || src.n_pages <= 0) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i) {
+        const Entry& e = cache[i];
+        if (e.k == src.k_pool && e.v == src.v_pool && e.n_kv == n_kv && e.d == d && e.n_pages == src.n_pages) {
+            *out = e.maps;
+            return e.ok;
+        }
+    }
+    Entry e{src.k_pool, src.v_pool, n_kv, d, src.n_pages, false, {}};
+    cudaPointerAttributes ak, av;
+    const bool dev = cudaPointerGetAttributes(&ak, src.k_pool) == cudaSuccess &&
+                     cudaPointerGetAttributes(&av, src.v_pool) == cudaSuccess && ak.type == cudaMemoryTypeDevice &&
+                     av.type == cudaMemoryTypeDevice;
+    cudaGetLastError();
+    if (dev) {
+        // the view spans exactly the pool's pages (the copy engine zero-fills
+        // anything outside a view's bounds)
+        const uint64_t dims[4] = {(uint64_t)d, 16, (uint64_t)n_kv, (uint64_t)src.n_pages};
+        const uint64_t strides[3] = {(uint64_t)d * 2, (uint64_t)16 * d * 2, (uint64_t)16 * d * 2 * n_kv};
+        const uint32_t box[4] = {64, 16, 1, 1};
+        e.ok = encode_bf16_map(&e.maps.k, src.k_pool, 4, dims, strides, box) == DKV_OK &&
+               encode_bf16_map(&e.maps.v, src.v_pool, 4, dims, strides, box) == DKV_OK;
+    }
+    cache[next] = e;
+    next = (next + 1) % 32;
+    n = n < 32 ? n + 1 : 32;
+    *out = e.maps;
+    return e.ok;
 }
 
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
@@ -506,7 +658,7 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
     if (a.src.dtype != DKV_BF16 || (dims.d != 64 && dims.d != 128) || a.split % kTcKT != 0) return DKV_OK;
     if (a.src.page_shift < 0) return DKV_OK;     // pages of any other size: generic kernel
     const int R = a.T * a.group;
-    a.n_rb = (R + kAttnRB - 1) / kAttnRB;
+    a.n_rb = R <= kAttnRB ? (R + kKqRows - 1) / kKqRows : (R + kAttnRB - 1) / kAttnRB;
     a.n_splits = (max_keys + a.split - 1) / a.split;
     if (a.n_splits < 1) a.n_splits = 1;
     const size_t n_tk = (size_t)dims.batch * dims.n_kv * a.n_rb;
@@ -521,13 +673,18 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
     dim3 grid(a.n_splits, dims.n_kv, dims.batch * a.n_rb);
     ProfScope ps(DKV_PROF_ATTN_FULL, 0.0, st);
     if (R <= kAttnRB) {
-        const int RT = (R + 7) / 8;
+        const int RT = (std::min(R, kKqRows) + 7) / 8;
         const int threads = 32 * kKqKG * RT;
+        KvMaps maps;
+        const bool tma = kv_maps(a.src, dims.n_kv, dims.d, &maps);
+        a.err = device_error_word();
         cudaError_t e = cudaSuccess;
-        if (dims.d == 128)
-            e = RT <= 4 ? launch_kq<128, 512>(a, grid, threads, st) : launch_kq<128, 1024>(a, grid, threads, st);
+        if (tma)
+            e = dims.d == 128 ? launch_kq<128, 256, true>(maps, a, grid, threads, st)
+                              : launch_kq<64, 256, true>(maps, a, grid, threads, st);
         else
-            e = RT <= 4 ? launch_kq<64, 512>(a, grid, threads, st) : launch_kq<64, 1024>(a, grid, threads, st);
+            e = dims.d == 128 ? launch_kq<128, 256, false>(maps, a, grid, threads, st)
+                              : launch_kq<64, 256, false>(maps, a, grid, threads, st);
         DKV_CUDA(e);
         *handled = true;
         return DKV_OK;

@@ -11,6 +11,7 @@ struct KeySrc {
     const void* v_pool;
     const int32_t* page_table;
     int page_size, max_pages, dtype;
+    int n_pages;             // pages in the pool (the bounds of the copy-engine view)
     int page_shift;          // log2(page_size), or -1 when page_size is not a power of two
     // drafter cache
     const uint8_t* k_codes;
@@ -42,6 +43,7 @@ struct AttnArgs {
     int note_mass;           // drafter: fold the attention mass into the slot scores
     float* score;            // drafter: [batch][n_layers][cap]
     unsigned* fold_tickets;  // [batch]
+    uint32_t* err;           // device error word (bounded waits of the copy-engine path)
 };
 
 constexpr int kAttnRB = 64;   // query rows (token x group head) per CTA

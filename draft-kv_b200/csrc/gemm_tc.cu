@@ -325,10 +325,37 @@ int get_encode(PFN_cuTensorMapEncodeTiled_v12000* fn) {
             q == cudaDriverEntryPointSuccess)
             g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
     });
-    DKV_REQUIRE(g_encode, "dkv_gemm: cuTensorMapEncodeTiled is unavailable");
+    DKV_REQUIRE(g_encode, "cuTensorMapEncodeTiled is unavailable");
     *fn = g_encode;
     return DKV_OK;
 }
+
+}  // namespace
+
+// A bf16 tensor map with 128-byte swizzle, no interleave, zero fill (shared
+// by the attention kernels).
+int encode_bf16_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                    const uint32_t* box) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    DKV_TRY(get_encode(&enc));
+    DKV_REQUIRE(((uintptr_t)base & 15) == 0, "tensor map base not 16-byte aligned");
+    cuuint64_t d[5];
+    cuuint64_t st[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) st[i] = strides[i];
+    }
+    const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), d, st, bx,
+                           es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    DKV_REQUIRE(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return DKV_OK;
+}
+
+namespace {
 
 // Tensor maps of the token matrices, keyed by (address, N, K, box rows): the
 // activation buffers of a forward sit at fixed addresses, so a map is encoded

@@ -23,6 +23,7 @@ _DEVICE_NAMES = {
     "quantize": ".compress", "quantize_codes": ".compress", "FullKVCache": ".compress",
     "CompressedKVCache": ".compress", "DraftKVEngine": ".engine", "GenerationResult": ".engine",
     "RoundLog": ".engine", "GPT2": ".models", "LlamaLike": ".models", "from_config": ".models",
+    "load_llama": ".models", "load_safetensors": ".checkpoint", "save_safetensors": ".checkpoint",
 }
 
 
@@ -41,6 +42,6 @@ __all__ = [
     "FullKVCache", "GPT2", "GenerationResult", "LayerPlan", "LlamaLike", "OraclePolicy",
     "PagedKVCache", "RoundLog", "ThompsonController", "best_gamma", "best_gamma_profile",
     "default_arms", "expected_tokens", "expected_tokens_profile", "from_config", "gamma_range",
-    "plan_blocks_needed", "quantize", "quantize_codes",
+    "plan_blocks_needed", "quantize", "quantize_codes", "load_llama", "load_safetensors", "save_safetensors",
 ]
 __version__ = "0.1.0"

@@ -1,23 +1,31 @@
 """CostModel constants measured on the device (reference throughput.py:77-81).
 
-The reference's CostModel prices a round from bytes moved plus fixed
-constants whose defaults describe an H100-class device: fixed_draft (launch
-and sampling overhead of a draft step), fixed_verify (of a verify pass) and
-resync_per_token (rewriting one accepted position into the drafter cache,
-also used for the cost of a configuration switch).  `calibrate_cost_model`
-replaces them with CUDA-event timings of this device's own rounds, so that
-`select()` gates drafting, and `ceiling()` bounds the speedup, with the
-device's real per-round overheads:
+The reference's CostModel prices a round from bytes moved at `bandwidth`
+plus fixed constants whose defaults describe an H100-class device:
+fixed_draft (launch and sampling overhead of a draft step), fixed_verify (of
+a verify pass) and resync_per_token (rewriting one accepted position into the
+drafter cache, also the cost of a configuration switch).
+`calibrate_cost_model` fits them to CUDA-event timings of this device's own
+rounds, so that `select()` gates drafting with the device's real costs:
 
-  fixed_draft  = measured draft step - (weights + drafter KV bytes) / bandwidth
-                 - compute_per_token
-  fixed_verify = measured verify pass - (weights + full KV bytes) / bandwidth
-                 - (gamma + 1) compute_per_token
+  bandwidth    = bytes of a verify pass (weights + full KV) / measured time:
+                 the device's effective rate (its kernels reach a fraction
+                 of the copy peak, and that fraction multiplies every byte);
+  fixed_verify = 0 (the verify pass defines the rate);
+  fixed_draft  = measured draft step - (weights + drafter KV) / bandwidth,
+                 clamped at 0 (a drafter that streams its bytes faster than
+                 the verify pass is priced at the verify pass's rate);
+  compute_per_token = 0 (the measured times include the arithmetic);
   resync_per_token  = measured resync of a round / tokens emitted per sequence
   rebuild_per_token = measured partial rebuild / (ctx x changed layers / layers)
 
-(each clamped at 0).  The draft step includes the on-device sampling and the
-verify pass the acceptance kernel, as the reference's constants do.
+With the full cache in host memory (full_kv_bandwidth below bandwidth) the
+verify pass is priced by the host link, so there the draft step defines the
+rate and fixed_verify is the verify pass's residual.  Fitting constant
+offsets instead would price an arm's extra bytes at the copy peak: a 16-bit
+drafter kept whole would look cheaper than the verify pass it equals.  The
+draft step includes the on-device sampling and the verify pass the
+acceptance kernel, as the reference's constants do.
 """
 
 from __future__ import annotations
@@ -81,16 +89,25 @@ def fit_constants(cm: CostModel, cfg, gamma: int, ctx: int, t_draft: float, t_ve
     docstring): a draft step, a (gamma+1)-token verify pass, the resync of a
     round that emitted `tokens_per_round` tokens per sequence, and a rebuild
     of `rebuild_layers` layers at context ctx."""
-    w = cm.weight_bytes / cm.bandwidth
-    fixed_draft = max(0.0, t_draft - (w + cm._kv_read_time(cm.draft_kv_bytes(cfg, ctx)) + cm.compute_per_token))
-    fixed_verify = max(0.0, t_verify - (w + cm.full_kv_bytes(ctx) / cm.full_kv_bandwidth
-                                        + (gamma + 1) * cm.compute_per_token))
+    b_draft = cm.weight_bytes + cm.draft_kv_bytes(cfg, ctx)
+    b_kv = cm.full_kv_bytes(ctx)
+    if cm.full_kv_bandwidth < cm.bandwidth:      # full cache over the host link
+        bw = b_draft / max(t_draft, 1e-12)
+        fixed_draft = 0.0
+        fixed_verify = max(0.0, t_verify - cm.weight_bytes / bw - b_kv / cm.full_kv_bandwidth)
+        full_bw = cm.full_kv_bandwidth
+    else:
+        bw = (cm.weight_bytes + b_kv) / max(t_verify, 1e-12)
+        fixed_verify = 0.0
+        fixed_draft = max(0.0, t_draft - b_draft / bw)
+        full_bw = bw
     resync_per_token = max(0.0, t_resync) / max(tokens_per_round, 1e-9)
     rebuild_per_token = (t_rebuild / (ctx * rebuild_layers / cm.n_layers)
                          if t_rebuild > 0 and ctx > 0 and rebuild_layers > 0 else None)
-    out = replace(cm, fixed_draft=fixed_draft, fixed_verify=fixed_verify, resync_per_token=resync_per_token,
-                  rebuild_per_token=rebuild_per_token)
+    out = replace(cm, bandwidth=bw, full_kv_bandwidth=full_bw, compute_per_token=0.0, fixed_draft=fixed_draft,
+                  fixed_verify=fixed_verify, resync_per_token=resync_per_token, rebuild_per_token=rebuild_per_token)
     meas = dict(cfg=cfg.label(), gamma=gamma, ctx=ctx, t_draft_step_s=t_draft, t_verify_s=t_verify,
+                bandwidth=bw, copy_peak=cm.bandwidth,
                 t_resync_s=t_resync, t_rebuild_s=t_rebuild, rebuild_layers=rebuild_layers,
                 tokens_per_round=tokens_per_round, fixed_draft=fixed_draft, fixed_verify=fixed_verify,
                 resync_per_token=resync_per_token, rebuild_per_token=rebuild_per_token)

@@ -192,6 +192,19 @@ class DeviceDecoder:
         self._graphs[key] = g
         g.replay()
 
+    @classmethod
+    def from_dir(cls, d, **kw) -> "DeviceDecoder":
+        """A model directory (config.json + model.safetensors or shards), as
+        the reference's GPT2.from_dir / LlamaLike.from_dir (gpt2.py:167-172,
+        llama.py:153-156); weights go straight to the device in their stored
+        dtype.  `dtype` overrides the checkpoint's (bf16 for bfloat16 / float16
+        checkpoints, f32 otherwise)."""
+        from .checkpoint import load_config, load_dir_weights
+        cfg = load_config(d)
+        if "dtype" in kw:
+            cfg["dtype"] = kw.pop("dtype")
+        return cls(load_dir_weights(d, device=kw.get("device", "cuda")), cfg, **kw)
+
     def forward(self, tokens, cache, start_pos: int):
         """Run `tokens` at positions [start_pos, start_pos + T) against `cache`
         (a device FullKVCache / PagedKVCache, or a CompressedKVCache for a
@@ -388,6 +401,16 @@ def random_device_weights(cfg: dict, seed: int = 0, std: float = 0.02, device: s
             w[p + "mlp.c_proj.weight"], w[p + "mlp.c_proj.bias"] = R(F, d), zeros(d)
         w["ln_f.weight"], w["ln_f.bias"] = ones(d), zeros(d)
     return w
+
+
+def load_llama(d):
+    """(model, tokenizer) for a Llama / Qwen2 checkpoint directory
+    (llama.py:228-234); the tokenizer is not part of the device build and is
+    returned as None."""
+    from pathlib import Path
+    if not (Path(d) / "model.safetensors").exists() and not (Path(d) / "model.safetensors.index.json").exists():
+        raise FileNotFoundError(f"no checkpoint at {d}")
+    return LlamaLike.from_dir(d), None
 
 
 def from_config(weights: dict, config: dict, **kw) -> DeviceDecoder:

@@ -69,13 +69,16 @@ def small_model_weights(W, name):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
-    ap.add_argument("--only", choices=["adaptive"], default=None,
+    ap.add_argument("--only", choices=["adaptive", "safetensors"], default=None,
                     help="write only this fixture (the others are left as they are)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     import draftkv as ref                          # the reference package
     if args.only == "adaptive":
         adaptive_fixtures(ref)
+        return
+    if args.only == "safetensors":
+        safetensors_fixture()
         return
     from draftkv import compress as rc
     from draftkv.gpt2 import GPT2
@@ -241,7 +244,30 @@ def main():
                            free=list(map(int, pk.pool._free)), frag=pk.fragmentation()))
     (HERE / "paged_trace.json").write_text(json.dumps(ptrace))
     adaptive_fixtures(ref)
+    safetensors_fixture()
     print("golden fixtures written to", HERE)
+
+
+def safetensors_fixture():
+    """A small safetensors file (F32, F16, BF16, I64 tensors and metadata)
+    written by the device build's writer, and what the reference's reader
+    (gpt2.py:25-46) decodes from it."""
+    import torch
+    from draftkv.gpt2 import load_safetensors as ref_load
+    spec = importlib.util.spec_from_file_location("dkv_checkpoint", REPO / "draft-kv_b200" / "draftkv" / "checkpoint.py")
+    ck = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ck)
+    rng = np.random.default_rng(41)
+    tensors = {
+        "a.f32": rng.standard_normal((3, 5)).astype(np.float32),
+        "b.f16": rng.standard_normal((7,)).astype(np.float16),
+        "c.bf16": torch.from_numpy(rng.standard_normal((4, 6)).astype(np.float32)).to(torch.bfloat16),
+        "d.i64": np.arange(-3, 5, dtype=np.int64).reshape(2, 4),
+    }
+    path = HERE / "tiny.safetensors"
+    ck.save_safetensors(tensors, path, metadata={"format": "pt"})
+    got = ref_load(path)
+    np.savez_compressed(HERE / "tiny_safetensors_ref.npz", **{k.replace(".", "_"): v for k, v in got.items()})
 
 
 # ---------------------------------------------------------------- adaptive allocator

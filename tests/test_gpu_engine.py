@@ -294,3 +294,29 @@ def test_partial_rebuild_leaves_other_layers_untouched():
     assert comp.cfgs[1] == CompressionConfig(4, 0.25)
     for L in range(m.n_layers):
         assert np.array_equal(comp.read(L)[0], before[L]) == (L != 1), L
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("name", list(SMALL_MODELS))
+def test_checkpoint_directory_matches_oracle(tmp_path, golden, name, dtype):
+    """A HuggingFace-style directory (config.json + model.safetensors, fp32 or
+    bf16 tensors) through from_dir, against the oracle fed the reference
+    reader's decoding of the same file (fp32 numpy): logits within the
+    configuration's tolerance."""
+    from draftkv import FullKVCache, GPT2, LlamaLike
+    from draftkv.checkpoint import load_safetensors, save_safetensors
+    meta, _ = golden
+    cfg = {k: v for k, v in small_model_cfg(W, name).items() if k != "dtype"}
+    cfg["torch_dtype"] = "bfloat16" if dtype == "bf16" else "float32"
+    wts = small_model_weights(W, name)
+    if dtype == "bf16":
+        wts = {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in wts.items()}
+    save_safetensors(wts, tmp_path / "model.safetensors", metadata={"format": "pt"})
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    m = (GPT2 if "n_embd" in cfg else LlamaLike).from_dir(tmp_path)
+    assert (m.dtype == 1) == (dtype == "bf16")
+    om = oracle.OracleModel(load_safetensors(tmp_path / "model.safetensors"), cfg)
+    prompt = meta[name]["prompt"]
+    got = m.forward(np.array(prompt), FullKVCache(m.n_layers), 0).cpu().numpy()
+    want = om.forward(np.array(prompt), oracle.OracleFull(om.n_layers), 0)
+    assert rel_err(got, want) < TOL[dtype]

@@ -430,3 +430,39 @@ def test_drafter_capacity_is_whole_tiles():
     assert comp.cap % 16 == 0 and comp.cap >= 1000
     comp._grow(2049)
     assert comp.cap % 16 == 0 and comp.cap >= 2049
+
+
+def test_full_attention_reads_pages_anywhere_in_a_large_pool():
+    """Pages far into a large pool (ids above 2^31 elements / page size, as a
+    32-layer, 4-sequence, 32k-context pool has) are read correctly by the
+    copy-engine path: T = 1 attention over 40 pages of ids 139900.. against a
+    torch fp32 reference (1e-2, bf16 operands)."""
+    from draftkv import PagedKVCache
+    L = lib()
+    n_kv, d, G, n = 8, 128, 4, 640
+    cache = PagedKVCache(1, n_kv, d, 16, 140000, "bf16", batch=1, max_blocks_per_seq=64)
+    pages = list(range(139900, 139900 + n // 16 + 1))
+    cache.block_tables[0][0] = list(pages)
+    for i, p in enumerate(pages):
+        cache.table_host[0, 0, i] = p
+    cache._dirty = True
+    rng = np.random.default_rng(5)
+    k = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    v = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    src = torch.from_numpy(np.stack([k, v], axis=2)).to("cuda", torch.bfloat16)
+    p0 = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    L.call("dkv_full_write", cache.struct(), cache.dims(), 0, src.data_ptr(), n, p0.data_ptr(), None, L.stream_ptr())
+    cache.set_length(0, n)
+    q = torch.from_numpy(rng.standard_normal((1, n_kv * G, d)).astype(np.float32)).cuda()
+    pos0 = torch.tensor([n - 1], dtype=torch.int32, device="cuda")
+    dims = cache.dims()
+    work = torch.zeros(int(L.load().dkv_attn_work_bytes(dims, G, 1, cache.capacity_tokens, 128, 0)),
+                       dtype=torch.uint8, device="cuda")
+    out = torch.zeros((1, n_kv * G * d), dtype=torch.float32, device="cuda")
+    L.call("dkv_attn_full", cache.struct(), dims, 0, G, 1, q.data_ptr(), pos0.data_ptr(), out.data_ptr(), L.F32,
+           128, work.data_ptr(), work.numel(), L.stream_ptr())
+    kk = torch.from_numpy(k).cuda().repeat_interleave(G, dim=1)
+    vv = torch.from_numpy(v).cuda().repeat_interleave(G, dim=1)
+    s = torch.einsum("qhd,khd->qhk", q, kk) / np.sqrt(d)
+    ref = torch.einsum("qhk,khd->qhd", torch.softmax(s, -1), vv).reshape(1, -1)
+    torch.testing.assert_close(out, ref, rtol=1e-2, atol=1e-2)

@@ -23,7 +23,9 @@ pay is a transient of the first rounds of a long-running decode, not its
 steady state.  The settle rounds are device-timed on their own and reported
 under "explore"; the K timed steps measure the converged controller.  A
 shorter run of rounds follows with per-launch CUDA events (kernel shares and
-the GEMM roofline).
+the GEMM roofline), then a leg that always drafts (8-bit keep-1 arm, gamma
+2; "fixed_arm"), so every run times drafting rounds whatever the controller
+chose.
 
 Then the same prompts are decoded again from the start with gamma 0 (plain
 full-KV decoding, no drafter cache): every token the speculative rounds
@@ -358,7 +360,8 @@ def run_gpu(args) -> None:
     settle = 0 if "fixed" in conf else args.settle
     timed_n = args.steps * R
     prof_n = min(timed_n, args.prof_rounds)
-    spec_rounds = args.warmup * R + settle + timed_n + prof_n + 8      # + calibration rounds
+    fixed_n = 0 if ("fixed" in conf or args.no_fixed_arm) else min(timed_n, args.fixed_rounds)
+    spec_rounds = args.warmup * R + settle + timed_n + prof_n + fixed_n + 8      # + calibration rounds
     max_new = spec_rounds * (G + 1) + 8
     # keys per attention split: fixed for the model for the whole run (verify
     # and decode rows then share split boundaries).  When the (sequence, KV
@@ -520,6 +523,19 @@ def run_gpu(args) -> None:
         _lib.check(lib.dkv_prof_summary(i, C.byref(ms), C.byref(n), C.byref(by)), "dkv_prof_summary")
         prof[nm] = dict(ms=ms.value, launches=n.value, bytes=by.value)
     prof_launches = sum(v["launches"] for v in prof.values())
+    # a leg that always drafts: the 8-bit keep-1 arm at gamma 2 (the arm whose
+    # acceptance random weights leave high), so that every run, at every N,
+    # times drafting rounds whatever the controller chose
+    fixed_leg = None
+    if fixed_n:
+        saved_ctrl = engine.controller
+        engine.controller = FixedPolicy(CompressionConfig(8, 1.0), 2)
+        sess.round()                              # the drafter cache switches to the arm
+        f_start = [len(t) for t in sess.toks]
+        ftoks, fdev_s, _, _, _, _, _ = timed_rounds(sess, fixed_n, profile=False)
+        engine.controller = saved_ctrl
+        fixed_leg = dict(tokens=ftoks, dev_s=fdev_s,
+                         tpr=sum(len(t) - n for t, n in zip(sess.toks, f_start)) / max(1, fixed_n) / B)
     sess.finish()
     spec_streams = [list(t) for t in sess.toks]
     plen = len(prompts[0])
@@ -590,6 +606,19 @@ def run_gpu(args) -> None:
         explore["tokens_per_s"] = round(xv[0].item() / xv[1].item(), 3)
     base_tps = btoks_all / bdev_s
     speedup = value / base_tps
+    fixed_line = None
+    if fixed_leg is not None:
+        fv = torch.tensor([fixed_leg["tokens"], fixed_leg["dev_s"]], dtype=torch.float64, device="cuda")
+        if world > 1:
+            fs = fv.clone()
+            dist.all_reduce(fs, op=dist.ReduceOp.SUM)
+            fm = fv.clone()
+            dist.all_reduce(fm, op=dist.ReduceOp.MAX)
+            fv = torch.stack([fs[0], fm[1]])
+        ftps = fv[0].item() / fv[1].item()
+        fixed_line = {"cfg": "8b/keep1", "gamma": 2, "rounds": fixed_n, "tokens_per_s": round(ftps, 3),
+                      "speedup_vs_full_kv": round(ftps / base_tps, 4),
+                      "tokens_per_round_per_seq": round(fixed_leg["tpr"], 3)}
     top_cfg = max(cfg_counts.items(), key=lambda kv: kv[1])[0] if cfg_counts else CompressionConfig(4, 0.25)
     # the benchmark's target is stated against the 4-bit keep-0.25 arm's ceiling
     target_cfg = CompressionConfig(4, 0.25)
@@ -651,6 +680,7 @@ def run_gpu(args) -> None:
         "exchange": (f"batched async all-gather: every {exchange.period} rounds, applied {exchange.lag} rounds later, "
                      f"{exchange.batches} batches" if exchange is not None else None),
         "cost_model_calibration": calib,
+        "fixed_arm": fixed_line,
         "controller_settle_rounds": settle,
         "explore": ({"rounds": explore["rounds"], "tokens_per_s": explore["tokens_per_s"],
                      "speedup_vs_full_kv": round(explore["tokens_per_s"] / base_tps, 4)} if explore else None),
@@ -919,6 +949,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--rounds-per-step", type=int, default=10,
                     help="draft/verify rounds in one step (the step is the timed unit)")
+    ap.add_argument("--fixed-rounds", type=int, default=100,
+                    help="rounds of the always-drafting leg (8b/keep1, gamma 2)")
+    ap.add_argument("--no-fixed-arm", action="store_true", help="skip the always-drafting leg")
     ap.add_argument("--prof-rounds", type=int, default=60,
                     help="rounds timed again with per-launch CUDA events (kernel roofline)")
     ap.add_argument("--config", default="c4", choices=list(CONFIGS))

@@ -297,6 +297,9 @@ constexpr int kKqNST = 3;
 // more CTAs per (split, head), whose tiles the later ones mostly find in L2.
 // A row's arithmetic is the same in any CTA.
 constexpr int kKqRows = 16;
+// Page ids a CTA stages in shared memory (splits of up to 8192 keys; longer
+// splits look each page up in global memory).
+constexpr int kKqSplitPages = 512;
 
 template <int D>
 size_t kq_smem(int RT) {
@@ -350,6 +353,9 @@ __global__ void __launch_bounds__(MAXT, 2) attn_kq_kernel(const __grid_constant_
     __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(tsm);      // [NST][K 64xD | V 64xD]
     __shared__ float ms[kAttnRB], ls[kAttnRB];
     __shared__ __align__(8) uint64_t full_bar[kKqNST];
+    // page ids of this CTA's key split, staged once (copy-engine path): the
+    // producer thread then issues a tile's copies without a global load
+    __shared__ int32_t split_pages[kKqSplitPages];
     if (TMA && threadIdx.x == 0) {
         for (int i = 0; i < kKqNST; ++i) mbar_init(&full_bar[i], 1);
         fence_async_shared();
@@ -406,6 +412,12 @@ __global__ void __launch_bounds__(MAXT, 2) attn_kq_kernel(const __grid_constant_
 
     const int ntiles = k1 > k0 ? (k1 - k0 + kTcKT - 1) / kTcKT : 0;
     const int psh = src.page_shift, pmask = src.page_size - 1;     // power-of-two pages (host-checked)
+    const int n_split_pages = k1 > k0 ? (k1 - k0 + 15) / 16 : 0;
+    const bool staged = TMA && n_split_pages <= kKqSplitPages;
+    if (staged) {
+        for (int i = threadIdx.x; i < n_split_pages; i += nthreads) split_pages[i] = __ldg(ptab + (k0 >> 4) + i);
+        __syncthreads();
+    }
     auto load_tile = [&](int slot, int t0) {
         __nv_bfloat16* kd = ring + (size_t)slot * 2 * kTcKT * D;
         __nv_bfloat16* vd = kd + kTcKT * D;
@@ -416,7 +428,7 @@ __global__ void __launch_bounds__(MAXT, 2) attn_kq_kernel(const __grid_constant_
                 const int np = min(kTcKT / 16, (k1 - t0 + 15) / 16);
                 mbar_expect_tx(&full_bar[slot], (uint32_t)np * 2 * (D / 64) * (16 * 64 * 2));
                 for (int j = 0; j < np; ++j) {
-                    const int page = __ldg(ptab + ((t0 >> 4) + j));
+                    const int page = staged ? split_pages[((t0 - k0) >> 4) + j] : __ldg(ptab + ((t0 >> 4) + j));
 #pragma unroll
                     for (int x = 0; x < D / 64; ++x) {
                         tma_load_4d(kd + x * (kTcKT * 64) + j * 16 * 64, &maps.k, x * 64, 0, h, page, &full_bar[slot]);

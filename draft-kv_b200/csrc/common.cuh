@@ -102,12 +102,6 @@ inline cudaError_t allow_smem_max_once() {
     return once.run([] { return allow_smem_max(Kern); });
 }
 
-// Programmatic dependent launch.  A kernel launched with launch_pdl() may
-// start while the previous kernel on the stream is still running: it must
-// execute pdl_wait() before it reads anything an earlier kernel wrote or
-// writes anything an earlier kernel reads.  pdl_trigger() lets the next
-// kernel start early (it still waits for this one to complete in its own
-// pdl_wait()).  Both are no-ops for kernels launched the ordinary way.
 // Bytes of one drafter-cache vector of d elements at `bits` per element
 // (16: raw entries of raw_dtype).  A layer's vectors are stored densely at
 // this stride inside each (sequence, layer, head) region of cap x cb_max
@@ -152,6 +146,12 @@ DKV_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
     return false;
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl() may
+// start while the previous kernel on the stream is still running: it must
+// execute pdl_wait() before it reads anything an earlier kernel wrote or
+// writes anything an earlier kernel reads.  pdl_trigger() lets the next
+// kernel start early (it still waits for this one to complete in its own
+// pdl_wait()).  Both are no-ops for kernels launched the ordinary way.
 DKV_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 DKV_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" :::); }
 

@@ -11,6 +11,13 @@
 namespace dkv {
 size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap, size_t* attn_bytes,
                     size_t* gemm_bytes);
+int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st);
+
+// RMSNorm fused into the GEMMs (bf16 Llama-family models): the norm before
+// the QKV, gate/up and head projections costs no launch of its own.
+bool fused_norm(const dkv_model* m) {
+    return m->arch == DKV_ARCH_LLAMA && m->dtype == DKV_BF16 && m->d_model % 128 == 0;
+}
 }
 
 using namespace dkv;
@@ -40,6 +47,10 @@ size_t dkv::forward_work(const dkv_model* m, int batch, int T, int max_ctx, int 
     b += align_up((size_t)N * dff_act * elem, 256);                  // act
     b += align_up((size_t)N * HD * 4, 256);                          // q
     b += align_up((size_t)N * KD * 2 * elem, 256);                   // kv stage
+    if (fused_norm(m)) {
+        b += align_up((size_t)N * m->d_model * 2, 256);              // bf16(h * w) of the next norm
+        b += align_up((size_t)(m->d_model / 128) * N * 4, 256);      // its per-row-tile sums of squares
+    }
     return b + align_up(g, 256) + align_up(a, 256) + 4096;
 }
 
@@ -81,12 +92,34 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
     DKV_REQUIRE(h && x && act && q && stage && gwork && awork, "dkv_forward: arena");
     dkv_dims dims{m->n_layers, KV, D, st->batch};
     const int group = H / KV;
+    // fused RMSNorm: xn = bf16(h * w) of the next norm and its partial sums
+    // of squares, written by the previous residual GEMM (by norm_prep for
+    // the first layer) and divided out by the GEMM that reads xn
+    const bool fused = fused_norm(m);
+    uint8_t* xn = fused ? ar.take<uint8_t>(NM * dm * 2) : nullptr;
+    float* npart = fused ? ar.take<float>((size_t)(dm / 128) * NM) : nullptr;
+    DKV_REQUIRE(!fused || (xn && npart), "dkv_forward: arena");
+    auto norm_in = [&](dkv_epilogue& e) {
+        if (!fused) return;
+        e.norm_in_part = npart;
+        e.norm_n_part = dm / 128;
+        e.norm_ld = (int)NM;
+        e.norm_dm = dm;
+        e.norm_eps = m->eps;
+    };
+    auto norm_out = [&](dkv_epilogue& e, const float* w_next) {
+        if (!fused) return;
+        e.norm_out_part = npart;
+        e.norm_out_x = xn;
+        e.norm_out_w = w_next;
+        e.norm_ld = (int)NM;
+    };
+    const uint8_t* xin = fused ? xn : x;    // what the normed projections read
 
-    DKV_TRY(dkv_embed(m->tok_emb, m->dtype, m->pos_emb, st->tokens, st->tok_stride, st->batch, st->T, st->pos0, dm,
-                      m->vocab, m->max_pos, h, stream));
-    for (int L = 0; L < m->n_layers; ++L) {
+    const int M_qkv = round128(HD + 2 * KD), M_up = round128(llama ? 2 * m->d_ff : m->d_ff);
+
+    auto qkv_epi = [&](int L) {
         const dkv_layer& ly = m->layers[L];
-        DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n1_w, ly.n1_b, m->eps, x, m->dtype, stream));
         dkv_epilogue e{};
         e.kind = DKV_EPI_QKV;
         e.bias = ly.b_qkv;
@@ -103,7 +136,57 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
         e.full = full;
         e.layer = L;
         e.n_layers = m->n_layers;
-        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_qkv, m->dtype, round128(HD + 2 * KD), N, dm, &e, gwork, gemm_bytes, stream));
+        norm_in(e);
+        return e;
+    };
+    auto o_epi = [&](int L) {
+        dkv_epilogue e{};
+        e.kind = DKV_EPI_RESADD;
+        e.bias = m->layers[L].b_o;
+        e.out_f32 = h;
+        e.ld_out = dm;
+        e.act_dtype = m->dtype;
+        norm_out(e, m->layers[L].n2_w);
+        return e;
+    };
+    auto up_epi = [&](int L) {
+        dkv_epilogue e{};
+        e.kind = llama ? DKV_EPI_SWIGLU : DKV_EPI_GELU;
+        e.bias = m->layers[L].b_up;
+        e.act = act;
+        e.act_dtype = m->dtype;
+        e.ld_out = m->d_ff;
+        norm_in(e);
+        return e;
+    };
+    auto down_epi = [&](int L) {
+        dkv_epilogue e{};
+        e.kind = DKV_EPI_RESADD;
+        e.bias = m->layers[L].b_down;
+        e.out_f32 = h;
+        e.ld_out = dm;
+        e.act_dtype = m->dtype;
+        norm_out(e, L + 1 < m->n_layers ? m->layers[L + 1].n1_w : m->nf_w);
+        return e;
+    };
+    auto head_epi = [&]() {
+        dkv_epilogue e{};
+        e.kind = DKV_EPI_STORE;
+        e.out_f32 = st->logits;
+        e.ld_out = m->vocab;
+        e.act_dtype = m->dtype;
+        norm_in(e);
+        return e;
+    };
+
+    DKV_TRY(dkv_embed(m->tok_emb, m->dtype, m->pos_emb, st->tokens, st->tok_stride, st->batch, st->T, st->pos0, dm,
+                      m->vocab, m->max_pos, h, stream));
+    if (fused) DKV_TRY(norm_prep(h, N, dm, m->layers[0].n1_w, xn, npart, (int)NM, (cudaStream_t)stream));
+    for (int L = 0; L < m->n_layers; ++L) {
+        const dkv_layer& ly = m->layers[L];
+        if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n1_w, ly.n1_b, m->eps, x, m->dtype, stream));
+        const dkv_epilogue e = qkv_epi(L);
+        DKV_TRY(dkv_gemm(xin, m->dtype, ly.w_qkv, m->dtype, M_qkv, N, dm, &e, gwork, gemm_bytes, stream));
         if (comp) {
             DKV_TRY(dkv_comp_append(comp, full, dims, L, 1, stage, m->dtype, 1, st->pos0, nullptr, nullptr, L == 0 ? 1 : 0,
                                     stream));
@@ -112,36 +195,16 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
             DKV_TRY(dkv_attn_full(full, dims, L, group, st->T, q, st->pos0, x, m->dtype, m->split_keys, awork,
                                   attn_bytes, stream));
         }
-        dkv_epilogue eo{};
-        eo.kind = DKV_EPI_RESADD;
-        eo.bias = ly.b_o;
-        eo.out_f32 = h;
-        eo.ld_out = dm;
-        eo.act_dtype = m->dtype;
+        const dkv_epilogue eo = o_epi(L);
         DKV_TRY(dkv_gemm(x, m->dtype, ly.w_o, m->dtype, round128(dm), N, HD, &eo, gwork, gemm_bytes, stream));
-        DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n2_w, ly.n2_b, m->eps, x, m->dtype, stream));
-        dkv_epilogue eu{};
-        eu.kind = llama ? DKV_EPI_SWIGLU : DKV_EPI_GELU;
-        eu.bias = ly.b_up;
-        eu.act = act;
-        eu.act_dtype = m->dtype;
-        eu.ld_out = m->d_ff;
-        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_up, m->dtype, round128(llama ? 2 * m->d_ff : m->d_ff), N, dm, &eu, gwork,
-                         gemm_bytes, stream));
-        dkv_epilogue ed{};
-        ed.kind = DKV_EPI_RESADD;
-        ed.bias = ly.b_down;
-        ed.out_f32 = h;
-        ed.ld_out = dm;
-        ed.act_dtype = m->dtype;
+        if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n2_w, ly.n2_b, m->eps, x, m->dtype, stream));
+        const dkv_epilogue eu = up_epi(L);
+        DKV_TRY(dkv_gemm(xin, m->dtype, ly.w_up, m->dtype, M_up, N, dm, &eu, gwork, gemm_bytes, stream));
+        const dkv_epilogue ed = down_epi(L);
         DKV_TRY(dkv_gemm(act, m->dtype, ly.w_down, m->dtype, round128(dm), N, m->d_ff, &ed, gwork, gemm_bytes, stream));
     }
-    DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, m->nf_w, m->nf_b, m->eps, x, m->dtype, stream));
-    dkv_epilogue eh{};
-    eh.kind = DKV_EPI_STORE;
-    eh.out_f32 = st->logits;
-    eh.ld_out = m->vocab;
-    eh.act_dtype = m->dtype;
-    DKV_TRY(dkv_gemm(x, m->dtype, m->w_head, m->dtype, m->vocab_pad, N, dm, &eh, gwork, gemm_bytes, stream));
+    if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, m->nf_w, m->nf_b, m->eps, x, m->dtype, stream));
+    const dkv_epilogue eh = head_epi();
+    DKV_TRY(dkv_gemm(xin, m->dtype, m->w_head, m->dtype, m->vocab_pad, N, dm, &eh, gwork, gemm_bytes, stream));
     return DKV_OK;
 }

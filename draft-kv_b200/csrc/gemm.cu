@@ -28,6 +28,7 @@ constexpr size_t kGemmTickets = 65536;
 uint32_t* device_error_word();
 // tensor-core GEMM (gemm_tc.cu)
 int choose_split_tc(int M, int K);
+
 int gemm_tc(const void* x, const void* w, int M, int N, int K, int S, const EpiArgs& epi, cudaStream_t st);
 int pack_weight_tc(const uint16_t* w, int M, int K, uint16_t* out, cudaStream_t st);
 size_t packed_weight_bytes_tc(int M, int K);
@@ -156,6 +157,21 @@ int epilogue_columns(const dkv_epilogue* epi, int M, int* M_real, const char* wh
                     "%s QKV: q_out/pos0 required and d_head must divide 128", who);
         DKV_REQUIRE(epi->kv_stage || (epi->full && epi->full->k_pool), "%s QKV: no K/V destination", who);
     }
+    if (epi->norm_in_part)
+        DKV_REQUIRE(epi->norm_n_part > 0 && epi->norm_dm > 0 && epi->norm_ld > 0,
+                    "%s: fused norm input needs norm_n_part, norm_dm and norm_ld", who);
+    if (epi->norm_out_x || epi->norm_out_part || epi->norm_out_w)
+        DKV_REQUIRE(epi->kind == DKV_EPI_RESADD && epi->norm_out_x && epi->norm_out_part && epi->norm_out_w &&
+                        epi->norm_ld > 0,
+                    "%s: fused norm output needs RESADD and norm_out_x, norm_out_part, norm_out_w, norm_ld", who);
+    return DKV_OK;
+}
+
+// The fused norm sides live in the tensor-core kernel's epilogue only.
+int fused_norm_bf16_only(const dkv_epilogue* epi, int w_dtype, int N, const char* who) {
+    const bool fused = epi->norm_in_part || epi->norm_out_x;
+    DKV_REQUIRE(!fused || w_dtype == DKV_BF16, "%s: fused RMSNorm needs bf16 weights", who);
+    DKV_REQUIRE(!fused || epi->norm_ld >= N, "%s: norm_ld (%d) < N (%d)", who, epi->norm_ld, N);
     return DKV_OK;
 }
 
@@ -184,6 +200,14 @@ dkv::EpiArgs dkv::make_epi(const dkv_epilogue* e, int M_real) {
     a.model_dtype = e->act_dtype;
     a.layer = e->layer;
     a.n_layers = e->n_layers;
+    a.norm_in_part = e->norm_in_part;
+    a.norm_n_part = e->norm_n_part;
+    a.norm_ld = e->norm_ld;
+    a.norm_dm = e->norm_dm;
+    a.norm_eps = e->norm_eps;
+    a.norm_out_part = e->norm_out_part;
+    a.norm_out_x = e->norm_out_x;
+    a.norm_out_w = e->norm_out_w;
     if (e->full) {
         a.k_pool = e->full->k_pool;
         a.v_pool = e->full->v_pool;
@@ -251,6 +275,7 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     if (N == 0) return DKV_OK;
     int M_real = M;
     DKV_TRY(epilogue_columns(epi, M, &M_real, "dkv_gemm"));
+    DKV_TRY(fused_norm_bf16_only(epi, w_dtype, N, "dkv_gemm"));
     const EpiArgs ea = make_epi(epi, M_real);
     cudaStream_t st = (cudaStream_t)stream;
     // algorithmic bytes: the weights once, the activations in and out
@@ -333,6 +358,7 @@ extern "C" int dkv_gemm_noalloc(const void* x, int x_dtype, const void* w, int w
     DKV_REQUIRE(K % 16 == 0, "dkv_gemm_noalloc: K (%d) must be a multiple of 16", K);
     int M_real = M;
     DKV_TRY(epilogue_columns(epi, M, &M_real, "dkv_gemm_noalloc"));
+    DKV_TRY(fused_norm_bf16_only(epi, w_dtype, N, "dkv_gemm_noalloc"));
     if (N == 0) return DKV_OK;
     const EpiArgs ea = make_epi(epi, M_real);
     cudaStream_t st = (cudaStream_t)stream;

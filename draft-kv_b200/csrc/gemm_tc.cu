@@ -48,7 +48,7 @@
 #include <algorithm>
 #include <mutex>
 
-#include "gemm_epilogue.cuh"
+#include "tcgen05.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -56,8 +56,6 @@ namespace dkv {
 
 uint32_t* device_error_word();
 
-constexpr int kTcKB = 64;                           // k elements per swizzle block
-constexpr int kTcBlockBytes = kTileM * kTcKB * 2;   // one 128 x 64 weight block: 16 KB
 constexpr int kTcStageKB = 2;                       // k blocks per stage (128 k)
 constexpr int kTcThreads = 128;
 
@@ -89,68 +87,6 @@ struct TcArgs {
     EpiArgs epi;
 };
 
-// ---- tcgen05 / tensor-copy primitives (inline PTX, sm_100a)
-DKV_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-DKV_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-DKV_DEV void tmem_alloc(uint32_t* slot, uint32_t cols) {   // whole warp
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
-                 "r"(cols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-}
-DKV_DEV void tmem_dealloc(uint32_t taddr, uint32_t cols) {   // whole warp
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(cols) : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024
-// bytes apart (stride byte offset), leading byte offset 16 (unused for this
-// layout), descriptor version 1.
-DKV_DEV uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
-}
-
-// Instruction descriptor of kind::f16: bf16 A and B, f32 D, both K-major,
-// M = 128, N = NB (a multiple of 16 up to 256).
-template <int NB>
-constexpr uint32_t tc_idesc() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NB >> 3) << 17) | ((128u >> 4) << 24);
-}
-
-template <int NB>
-DKV_DEV void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(tc_idesc<NB>()), "r"(accumulate)
-        : "memory");
-}
-// Arrives on `bar` once every MMA this thread issued so far has completed.
-DKV_DEV void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
-}
-DKV_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-}
-// 2-D tensor copy of one box (64 k x NB rows) into shared memory (no multicast).
-DKV_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-DKV_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
-
 template <int NB>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs g) {
     using Geo = TcGeo<NB>;
@@ -160,6 +96,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     __shared__ __align__(8) uint64_t empty_bar[NST];
     __shared__ __align__(8) uint64_t acc_bar;
     __shared__ uint32_t tmem_slot;
+    __shared__ float inv_s[NB];      // fused RMSNorm: 1 / rms of each token row
     uint8_t* ring = tc_raw + ((1024u - (smem_u32(tc_raw) & 1023u)) & 1023u);
     cg::cluster_group cluster = cg::this_cluster();
     const int S = g.S;
@@ -277,19 +214,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (S > 1) {
         cluster.sync();
         if (ok) {
-            for (int e = threadIdx.x; e < (j1 - j0) * kTileM; e += blockDim.x) {
-                const int o = (j0 + e / kTileM) * kTileStride + e % kTileM;
-                float v = cluster.map_shared_rank(tile, 0)[o];
-                for (int q = 1; q < S; ++q) v += cluster.map_shared_rank(tile, q)[o];
-                tile[o] = v;
+            // this CTA's token rows [j0, j1): the S partial tiles summed in
+            // rank order; the S loads of an element (two elements a pass) are
+            // issued before the sum
+            const float* rt[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) rt[q] = q < S ? cluster.map_shared_rank(tile, q) : tile;
+            const int cnt = (j1 - j0) * kTileM;
+            for (int e0 = threadIdx.x; e0 < cnt; e0 += 2 * kTcThreads) {
+                float v[2][8];
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int e = e0 + k * kTcThreads;
+                    const int o = (j0 + e / kTileM) * kTileStride + e % kTileM;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v[k][q] = (q < S && e < cnt) ? rt[q][o] : 0.f;
+                }
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int e = e0 + k * kTcThreads;
+                    if (e >= cnt) continue;
+                    float acc = v[k][0];
+#pragma unroll
+                    for (int q = 1; q < 8; ++q)
+                        if (q < S) acc += v[k][q];
+                    tile[(j0 + e / kTileM) * kTileStride + e % kTileM] = acc;
+                }
             }
         }
+        // done reading the other CTAs' tiles: they may leave once every CTA
+        // has arrived (waited for below, after this CTA's epilogue)
+        cluster_arrive();
         __syncthreads();
-        if (ok) run_epilogue(g.epi, tile, mtile, n0, nb, j0, j1);
-        cluster.sync();       // no CTA leaves while another reads its tile
-    } else if (ok) {
-        run_epilogue(g.epi, tile, mtile, n0, nb);
     }
+    if (ok) {
+        const bool norm_in = g.epi.norm_in_part != nullptr;
+        if (norm_in) {
+            epi_token_inv(g.epi, n0, j0, j1, inv_s);
+            __syncthreads();
+        }
+        run_epilogue(g.epi, tile, mtile, n0, nb, j0, j1, norm_in ? inv_s : nullptr);
+        if (g.epi.norm_out_x) {
+            __syncthreads();
+            epi_norm_partials(g.epi, tile, mtile, n0, j0, j1);
+        }
+    }
+    if (S > 1) cluster_wait();    // no CTA leaves while another reads its tile
 }
 
 // Packs W [M][K] bf16 into the layout above (2-byte elements).
@@ -355,11 +325,10 @@ int encode_bf16_map(CUtensorMap* m, const void* base, int rank, const uint64_t* 
     return DKV_OK;
 }
 
-namespace {
-
 // Tensor maps of the token matrices, keyed by (address, N, K, box rows): the
 // activation buffers of a forward sit at fixed addresses, so a map is encoded
 // once and reused.
+namespace {
 struct MapEntry {
     const void* x;
     int N, K, NB;
@@ -368,6 +337,8 @@ struct MapEntry {
 std::mutex g_map_mu;
 MapEntry g_maps[256];
 int g_map_n = 0, g_map_next = 0;
+
+}  // namespace
 
 int token_map(const void* x, int N, int K, int NB, CUtensorMap* out) {
     std::lock_guard<std::mutex> lock(g_map_mu);
@@ -400,6 +371,8 @@ int token_map(const void* x, int N, int K, int NB, CUtensorMap* out) {
     return DKV_OK;
 }
 
+namespace {
+
 template <int NB>
 cudaError_t tc_attrs() {
     static DeviceOnce once;
@@ -412,7 +385,7 @@ cudaError_t tc_attrs() {
 }
 
 // Clusters of S CTAs of the kernel that can be resident at once on the
-// current device (one CTA per SM; a cluster stays inside one GPC).
+// current device (a cluster stays inside one GPC).
 int tc_active(int S) {
     static int cache[64][9] = {};
     int dev = 0;
@@ -435,7 +408,10 @@ int tc_active(int S) {
             cudaGetLastError();
             return 0;
         }
-        cache[dev][S] = n;
+        // the query counts one CTA of the kernel per SM, while two of its
+        // ~110 KB CTAs run on an SM at once (measured on B200: 256 CTAs of a
+        // 4096 x 4096 launch start within 2 us on 142 SMs)
+        cache[dev][S] = 2 * n;
     }
     return cache[dev][S];
 }
@@ -463,19 +439,26 @@ cudaError_t tc_launch(const CUtensorMap& map, const TcArgs& g, int mtiles, int n
 
 }  // namespace
 
-// K split of the tensor-core GEMM for an (M, K) weight: the S in 1..8 (at
-// most the number of 64-wide k blocks) that minimises the modelled time of
-// one CTA in k16 steps, rounds x (ceil(KB / S) x 4 + 32), where rounds = row
-// tiles per cluster with as many clusters as fit at once and 32 k16 steps
-// charge a CTA's fixed costs (launch, first copies landing, epilogue), plus 8
-// per extra partial summed.  Depends on (M, K) and the device only.
+// K split of the tensor-core GEMM for an (M, K) weight: the S in {1, 2, 4, 8}
+// (at most the number of 128-wide k stages) that minimises the modelled time
+// of one CTA in k16 steps, rounds x (ceil(KB / S) x 4 + 32), where rounds =
+// row tiles per cluster with as many clusters as fit at once and 32 k16
+// steps charge a CTA's fixed costs (launch, first copies landing, epilogue),
+// plus 8 per extra partial summed; 1 when the row tiles alone outnumber the
+// CTAs that fit at once.  Depends on (M, K) and the device only.  Measured on
+// B200 (decode chains of QKV, O, gate/up, down under programmatic dependent
+// launch, N = 4 and 8): splits 4, 4, 1, 4 of the Llama-3-8B layer within 2 %
+// of the best of the sweep.
 int choose_split_tc(int M, int K) {
     const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
     const int KB = (K + kTcKB - 1) / kTcKB;
     const int max_s = std::max(1, std::min(8, KB / kTcStageKB));
+    // more row tiles than CTAs fit at once: the weight stream already fills
+    // the GPU, a split only adds partial sums
+    if (mtiles >= tc_active(1)) return 1;
     int best = 1;
     double best_cost = 0.0;
-    for (int S = 1; S <= max_s; ++S) {
+    for (int S = 1; S <= max_s; S *= 2) {
         const int act = tc_active(S);
         if (act <= 0) continue;
         const int ncl = std::min(mtiles, act);

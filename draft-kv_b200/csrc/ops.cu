@@ -449,6 +449,46 @@ extern "C" int dkv_embed(const void* emb, int emb_dtype, const void* pos_emb, co
     return DKV_OK;
 }
 
+// First half of a fused RMSNorm (the forward's first layer; later ones come
+// out of the residual GEMM's epilogue): x[n][m] = bf16(h[n][m] * w[m]) and
+// part[t * ld + n] = sum of h[n][m]^2 over the 128 columns m of tile t, in
+// the order of the GEMM epilogue (4 columns a lane, then a butterfly).  The
+// GEMM that reads x divides by the rms.  One CTA of 4 warps per token.
+__global__ void __launch_bounds__(128) norm_prep_kernel(const float* __restrict__ h, int dm,
+                                                        const float* __restrict__ w, uint16_t* __restrict__ x,
+                                                        float* __restrict__ part, int ld) {
+    pdl_trigger();
+    pdl_wait();
+    const int n = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* row = h + (size_t)n * dm;
+    for (int t = warp; t < dm / 128; t += 4) {
+        const float* r = row + t * 128;
+        const float a = r[lane], b = r[lane + 32], c = r[lane + 64], d = r[lane + 96];
+        float v = ((a * a + b * b) + c * c) + d * d;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) part[(size_t)t * ld + n] = v;
+        const float* wt = w + t * 128;
+        uint16_t* xt = x + (size_t)n * dm + t * 128;
+        xt[lane] = f32_to_bf16_bits(a * wt[lane]);
+        xt[lane + 32] = f32_to_bf16_bits(b * wt[lane + 32]);
+        xt[lane + 64] = f32_to_bf16_bits(c * wt[lane + 64]);
+        xt[lane + 96] = f32_to_bf16_bits(d * wt[lane + 96]);
+    }
+}
+
+namespace dkv {
+int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st) {
+    DKV_REQUIRE(h && w && x && part && dm % 128 == 0 && ld >= N, "norm_prep args");
+    if (N == 0) return DKV_OK;
+    ProfScope ps(DKV_PROF_NORM, (double)N * dm * 6.0, st);
+    DKV_CUDA(launch_pdl(norm_prep_kernel, dim3(N), dim3(128), 0, st, h, dm, w, reinterpret_cast<uint16_t*>(x), part,
+                        ld));
+    DKV_LAUNCHED();
+    return DKV_OK;
+}
+}  // namespace dkv
+
 extern "C" int dkv_norm(const float* h, int N, int dm, int layernorm, const float* w, const float* b, float eps,
                         void* x, int x_dtype, void* stream) {
     DKV_REQUIRE(h && w && x && N >= 0 && dm > 0, "dkv_norm args");

@@ -1,0 +1,99 @@
+// tcgen05 / tensor-copy primitives shared by the tensor-core GEMM kernels
+// (inline PTX, sm_100a), the packed weight layout's constants and the host
+// helpers both GEMM entry points use.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "gemm_epilogue.cuh"
+
+namespace dkv {
+
+uint32_t* device_error_word();
+
+constexpr int kTcKB = 64;                           // k elements per swizzle block
+constexpr int kTcBlockBytes = kTileM * kTcKB * 2;   // one 128 x 64 weight block: 16 KB
+
+// ---- tcgen05 / tensor-copy primitives (inline PTX, sm_100a)
+DKV_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+DKV_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+DKV_DEV void tmem_alloc(uint32_t* slot, uint32_t cols) {   // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+DKV_DEV void tmem_dealloc(uint32_t taddr, uint32_t cols) {   // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024
+// bytes apart (stride byte offset), leading byte offset 16 (unused for this
+// layout), descriptor version 1.
+DKV_DEV uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: bf16 A and B, f32 D, both K-major,
+// M = 128, N = NB (a multiple of 16 up to 256).
+template <int NB>
+constexpr uint32_t tc_idesc() {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NB >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+template <int NB>
+DKV_DEV void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(tc_idesc<NB>()), "r"(accumulate)
+        : "memory");
+}
+// Arrives on `bar` once every MMA this thread issued so far has completed.
+DKV_DEV void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+DKV_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+// 2-D tensor copy of one box (64 k x NB rows) into shared memory (no multicast).
+DKV_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+DKV_DEV void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+// The two halves of a cluster barrier: arrive (release: this thread's
+// earlier shared-memory accesses, local and remote, are done) and wait.
+DKV_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory"); }
+DKV_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory"); }
+
+// Named barrier over `count` threads (a multiple of 32) of the CTA.
+DKV_DEV void named_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---- host
+// K split of a weight (M, K) (1, 2, 4 or 8): depends on (M, K) and the
+// device only.
+int choose_split_tc(int M, int K);
+// Token tile of a launch (a multiple of 16).
+int tc_token_tile(int N);
+// The cached 2-D tensor map of a bf16 token matrix X [N][K] with a box of
+// 64 k x NB rows (128-byte swizzle, zero fill past N and K).
+int token_map(const void* x, int N, int K, int NB, CUtensorMap* out);
+
+}  // namespace dkv

@@ -45,7 +45,9 @@ class EpilogueS(C.Structure):
                 ("act_dtype", C.c_int), ("ld_out", C.c_int),
                 ("n_heads", C.c_int), ("n_kv", C.c_int), ("d_head", C.c_int), ("tokens_per_seq", C.c_int),
                 ("pos0", vp), ("rope_cos", vp), ("rope_sin", vp), ("q_out", vp), ("kv_stage", vp),
-                ("full", vp), ("layer", C.c_int), ("n_layers", C.c_int)]
+                ("full", vp), ("layer", C.c_int), ("n_layers", C.c_int),
+                ("norm_in_part", vp), ("norm_n_part", C.c_int), ("norm_ld", C.c_int), ("norm_dm", C.c_int),
+                ("norm_eps", C.c_float), ("norm_out_part", vp), ("norm_out_x", vp), ("norm_out_w", vp)]
 
 
 class LayerS(C.Structure):

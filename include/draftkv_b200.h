@@ -250,6 +250,21 @@ typedef struct {
     void* kv_stage;             /* [N][n_kv][d] K then V at +N*n_kv*d, or NULL */
     const dkv_full_cache* full; /* write K/V into this cache when kv_stage == NULL */
     int layer, n_layers;
+    /* Fused RMSNorm (draftkv/llama.py:93-94), bf16 weights only; all NULL /
+     * 0 when unused.  Input side: X holds bf16(h * w) (not yet divided by the
+     * rms) and token n's accumulators are multiplied by
+     * 1 / sqrt(sum_t norm_in_part[t * norm_ld + n] / norm_dm + norm_eps)
+     * (t < norm_n_part, summed in t order) before bias and epilogue.
+     * Output side (RESADD only): besides h, writes norm_out_x[n][m] =
+     * bf16(h_new[n][m] * norm_out_w[m]) (ld_out columns) and
+     * norm_out_part[(m / 128) * norm_ld + n] = sum of h_new^2 over the 128
+     * rows m of that row tile, the next GEMM's input side. */
+    const float* norm_in_part;
+    int norm_n_part, norm_ld, norm_dm;
+    float norm_eps;
+    float* norm_out_part;
+    void* norm_out_x;
+    const float* norm_out_w;
 } dkv_epilogue;
 
 /* Packed layout of a bf16 weight W [M][K] (M % 128 == 0 after padding,

@@ -262,6 +262,107 @@ def test_bf16_gemm_matches_torch_and_is_batch_invariant(M, K):
     assert torch.equal(outs[100][:64], outs[64])
 
 
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1024, 512)])
+@pytest.mark.parametrize("N", [4, 36])
+def test_fused_rmsnorm_epilogues(M, K, N):
+    """The two halves of the RMSNorm fused into the bf16 GEMM (llama.py:93-94).
+    Output side (RESADD): h_new = h + X W^T + b, xn = bf16(h_new * w) and the
+    sums of h_new^2 over each 128-row tile, against torch fp32.  Input side
+    (STORE) on those: Y = (xn W2^T) / rms(h_new) + b2 per token.  Both
+    shapes run the split-K cluster reduction (4096 x 4096) and the unsplit
+    kernel (1024 x 512); a token's results do not depend on N."""
+    L = lib()
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    W = (torch.randn((M, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    X = torch.randn((N, K), generator=g, device="cuda").to(torch.bfloat16)
+    h0 = torch.randn((N, M), generator=g, device="cuda") * 3
+    b = torch.randn(M, generator=g, device="cuda") * 0.1
+    wn = torch.rand(M, generator=g, device="cuda") + 0.5
+    W2 = (torch.randn((256, M), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    b2 = torch.randn(256, generator=g, device="cuda") * 0.1
+    eps = 1e-5
+    Wt, W2t = L.pack_weight(W), L.pack_weight(W2)
+    work = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    ld = N + 3
+    h = h0.clone()
+    xn = torch.zeros((N, M), dtype=torch.bfloat16, device="cuda")
+    part = torch.full((M // 128, ld), -1.0, device="cuda")
+    e = L.EpilogueS()
+    e.kind = L.EPI_RESADD
+    e.bias = b.data_ptr()
+    e.out_f32 = h.data_ptr()
+    e.ld_out = M
+    e.act_dtype = L.BF16
+    e.norm_out_part = part.data_ptr()
+    e.norm_out_x = xn.data_ptr()
+    e.norm_out_w = wn.data_ptr()
+    e.norm_ld = ld
+    L.call("dkv_gemm", X.data_ptr(), L.BF16, Wt.data_ptr(), L.BF16, M, N, K, C.byref(e), work.data_ptr(),
+           work.numel(), L.stream_ptr())
+    torch.cuda.synchronize()
+    h_ref = h0 + (X.float() @ W.float().t() + b)
+    torch.testing.assert_close(h, h_ref, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(xn.float(), (h * wn).to(torch.bfloat16).float(), rtol=0, atol=0)
+    sq = (h * h).view(N, M // 128, 128).sum(-1).t()
+    torch.testing.assert_close(part[:, :N], sq, rtol=1e-5, atol=1e-5)
+    assert torch.all(part[:, N:] == -1.0)
+    out = torch.zeros((N, 256), device="cuda")
+    e2 = L.EpilogueS()
+    e2.kind = L.EPI_STORE
+    e2.bias = b2.data_ptr()
+    e2.out_f32 = out.data_ptr()
+    e2.ld_out = 256
+    e2.act_dtype = L.BF16
+    e2.norm_in_part = part.data_ptr()
+    e2.norm_n_part = M // 128
+    e2.norm_ld = ld
+    e2.norm_dm = M
+    e2.norm_eps = eps
+    L.call("dkv_gemm", xn.data_ptr(), L.BF16, W2t.data_ptr(), L.BF16, 256, N, M, C.byref(e2), work.data_ptr(),
+           work.numel(), L.stream_ptr())
+    torch.cuda.synchronize()
+    inv = 1.0 / torch.sqrt((h * h).mean(-1, keepdim=True) + eps)
+    ref = (xn.float() @ W2.float().t()) * inv + b2
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    # the same tokens at N = 1: bit-identical rows
+    if N > 1:
+        h1 = h0[:1].clone()
+        xn1 = torch.zeros((1, M), dtype=torch.bfloat16, device="cuda")
+        part1 = torch.zeros((M // 128, 1), device="cuda")
+        e.out_f32, e.norm_out_x, e.norm_out_part, e.norm_ld = h1.data_ptr(), xn1.data_ptr(), part1.data_ptr(), 1
+        L.call("dkv_gemm", X[:1].contiguous().data_ptr(), L.BF16, Wt.data_ptr(), L.BF16, M, 1, K, C.byref(e),
+               work.data_ptr(), work.numel(), L.stream_ptr())
+        torch.cuda.synchronize()
+        assert torch.equal(h1[0], h[0]) and torch.equal(xn1[0], xn[0]) and torch.equal(part1[:, 0], part[:, 0])
+
+
+def test_fused_rmsnorm_rejects_f32_and_wrong_kinds():
+    L = lib()
+    lib_ = L.load()
+    x = torch.zeros((4, 256), device="cuda")
+    w = torch.zeros((128, 256), device="cuda")
+    out = torch.zeros((4, 128), device="cuda")
+    part = torch.zeros((2, 4), device="cuda")
+    work = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    e = L.EpilogueS()
+    e.kind = L.EPI_STORE
+    e.out_f32 = out.data_ptr()
+    e.ld_out = 128
+    e.norm_in_part = part.data_ptr()
+    e.norm_n_part, e.norm_ld, e.norm_dm = 2, 4, 256
+    rc = lib_.dkv_gemm(x.data_ptr(), L.F32, w.data_ptr(), L.F32, 128, 4, 256, C.byref(e), work.data_ptr(),
+                       work.numel(), L.stream_ptr())
+    assert rc != 0 and b"bf16" in lib_.dkv_last_error()
+    e2 = L.EpilogueS()
+    e2.kind = L.EPI_STORE
+    e2.out_f32 = out.data_ptr()
+    e2.ld_out = 128
+    e2.norm_out_x = out.data_ptr()
+    rc = lib_.dkv_gemm(x.data_ptr(), L.BF16, w.data_ptr(), L.BF16, 128, 4, 256, C.byref(e2), work.data_ptr(),
+                       work.numel(), L.stream_ptr())
+    assert rc != 0 and b"RESADD" in lib_.dkv_last_error()
+
+
 def test_f32_gemm_matches_torch():
     L = lib()
     M, K = 256, 192

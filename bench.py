@@ -581,6 +581,7 @@ def run_gpu(args) -> None:
     compared = agree(compared, dist.ReduceOp.SUM if world > 1 else None)
     del bsess
     model._graphs.clear()
+    chain = gemm_decode_chain(model, B, pk) if model.dtype == _lib.BF16 else None
 
     # reduce over ranks: max time, summed tokens
     vals = torch.tensor([toks, dev_s, wall_s, btoks, bdev_s], dtype=torch.float64, device="cuda")
@@ -705,7 +706,8 @@ def run_gpu(args) -> None:
                      "traffic_basis": ratio["basis"] if ratio else None,
                      "bytes_per_launch": round(bytes_per_launch),
                      "avg_launch_us": round(g["ms"] * 1e3 / max(1, g["launches"]), 2),
-                     "rounds_profiled": prof_n},
+                     "rounds_profiled": prof_n,
+                     "decode_chain": chain},
         "kernel_time_share": kernel_share,
         "gpu_launches": int(round(prof_launches / max(1, prof_n) * timed_n)),
         "gpu_launches_basis": f"{prof_launches} launches counted over {prof_n} profiled rounds, scaled to "
@@ -811,6 +813,70 @@ def run_reference(args) -> None:
         "wall_s": round(time.perf_counter() - t_start, 1),
     }
     print(json.dumps(line), flush=True)
+
+
+def gemm_decode_chain(model, N: int, pk: dict) -> dict:
+    """The weight GEMMs of one decode forward (every layer's QKV, O, gate/up,
+    down and the head, with the model's packed weights) back to back as the
+    forward launches them -- programmatic dependent launch, one CUDA graph --
+    at N tokens, store epilogues into scratch.  Device time of the graph over
+    the weights' bytes: the weight stream's rate with launches overlapped,
+    beside the per-launch CUDA-event figure of the profiled rounds (whose
+    event between every two launches serialises them)."""
+    import ctypes as C
+    import torch
+    from draftkv import _lib
+
+    dm, HD, KD, dff = model.d_model, model.n_heads * model.d_head, model.n_kv_heads * model.d_head, model.d_ff
+
+    def r128(x):
+        return (x + 127) // 128 * 128
+
+    shapes = {"w_qkv": (r128(HD + 2 * KD), dm), "w_o": (r128(dm), HD), "w_up": (r128(2 * dff), dm),
+              "w_down": (r128(dm), dff)}
+    seq = [(ly[k], *shapes[k]) for ly in model._keep[5] for k in ("w_qkv", "w_o", "w_up", "w_down")]
+    seq.append((model._keep[2], model.vocab_pad, dm))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    xs = {K: torch.randn((N, K), generator=g, device="cuda").to(torch.bfloat16) for _, _, K in seq}
+    outs = {M: torch.zeros((N, M), dtype=torch.float32, device="cuda") for _, M, _ in seq}
+    work = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    epis = []
+    for _, M, K in seq:
+        e = _lib.EpilogueS()
+        e.kind = _lib.EPI_STORE
+        e.out_f32 = outs[M].data_ptr()
+        e.ld_out = M
+        e.act_dtype = _lib.BF16
+        epis.append(e)
+
+    def run():
+        for (w, M, K), e in zip(seq, epis):
+            _lib.call("dkv_gemm", xs[K].data_ptr(), _lib.BF16, w.data_ptr(), _lib.BF16, M, N, K, C.byref(e),
+                      work.data_ptr(), work.numel(), _lib.stream_ptr())
+
+    run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    for _ in range(3):
+        graph.replay()
+    ts = []
+    for _ in range(5):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ms = statistics.median(ts)
+    by = sum(M * K * 2 + N * K * 2 + N * M * 4 for _, M, K in seq)
+    gbs = by / (ms / 1e3) / 1e9
+    del graph
+    return {"tokens": N, "launches": len(seq), "ms_per_forward": round(ms, 3), "bytes_per_forward": int(by),
+            "achieved": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+            "basis": "the forward's weight GEMMs back to back in one CUDA graph (PDL), device time"}
 
 
 def run_kernel(args) -> None:

@@ -72,6 +72,8 @@ import numpy as np  # noqa: E402
 CONFIGS = {
     "c4": dict(preset="llama3-8b", ctx=32768, batch=4, temperature=0.0, gamma_max=8,
                workload="llama3-8b-shape bf16, ctx 32768, 4 seq/GPU, greedy, Thompson controller"),
+    "c4f": dict(preset="llama3-8b", ctx=32768, batch=4, temperature=0.0, gamma_max=8, fixed=(8, 1.0, 2),
+                workload="llama3-8b-shape bf16, ctx 32768, 4 seq/GPU, greedy, fixed 8b/keep1 gamma 2 (every round drafts)"),
     "c3": dict(preset="smollm2-135m", ctx=2048, batch=16, temperature=1.0, gamma_max=8,
                arms=[(8, 1.0), (4, 0.5), (4, 0.25), (2, 0.25)],
                workload="smollm2-135m-shape bf16, prompt 2048, 16 seq/GPU, T=1.0, 4-arm Thompson"),

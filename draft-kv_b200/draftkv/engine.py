@@ -282,15 +282,24 @@ class DraftKVEngine:
         arms = getattr(self.controller, "arms", None) or [cfg]
         cfgs = [c for a in arms for c in layer_cfgs(a, m.n_layers)] + layer_cfgs(cfg, m.n_layers)
         max_bits = max(c.bits for c in cfgs)
-        cap = 0
-        for c in cfgs:
-            kept = max(int(round(c.keep_frac * st.max_ctx)), c.sink + c.recent)
-            cap = max(cap, min(kept, st.max_ctx))
-        cap += st.G + 4
+        cap = self._comp_slots(st, cfgs)
         comp = CompressedKVCache(m.n_layers, layer_cfgs(cfg, m.n_layers), batch=st.B, capacity=cap,
                                  max_bits=max_bits)
         comp.materialize(m.n_kv_heads, m.d_head, m.dtype)
         return comp
+
+    @staticmethod
+    def _comp_slots(st: _Batch, cfgs) -> int:
+        """Slots a drafter cache needs for per-layer configs `cfgs`."""
+        cap = 0
+        for c in cfgs:
+            kept = max(int(round(c.keep_frac * st.max_ctx)), c.sink + c.recent)
+            cap = max(cap, min(kept, st.max_ctx))
+        return cap + st.G + 4
+
+    def _comp_too_small(self, st: _Batch, cfgs) -> bool:
+        comp = st.comp
+        return max(c.bits for c in cfgs) > comp._max_bits or self._comp_slots(st, cfgs) > comp.cap
 
     def _rebuild(self, st: _Batch, layers: list, ctx_t, advance: bool) -> None:
         if not layers:
@@ -454,8 +463,15 @@ class Session:
         elif self.comp_cfg != cfg:
             old = layer_cfgs(self.comp_cfg, m.n_layers)
             new = layer_cfgs(cfg, m.n_layers)
-            changed = [L for L in range(m.n_layers) if old[L] != new[L]]
-            st.comp.set_cfgs(new)
+            if eng._comp_too_small(st, new):
+                # wider codes or a larger budget than the cache was sized for
+                # (a policy switched to an arm outside the controller's set):
+                # a new cache, every layer rebuilt
+                st.comp = eng._new_comp(st, cfg)
+                changed = list(range(m.n_layers))
+            else:
+                changed = [L for L in range(m.n_layers) if old[L] != new[L]]
+                st.comp.set_cfgs(new)
             ctx_t = torch.tensor([n[b] - 1 for b in range(B)], dtype=torch.int32, device=m.device)
             eng._rebuild(st, changed, ctx_t, advance=0 in changed)
             self.comp_cfg = cfg

@@ -171,6 +171,29 @@ def test_batch_matches_single_sequences(golden):
         assert base[b] == DraftKVEngine(m, seed=0).generate_baseline(prompts[b], 20, 0.0)
 
 
+def test_switch_to_a_wider_arm_regrows_the_drafter_cache(golden):
+    """A session whose policy moves to an arm with wider codes and a larger
+    budget than its drafter cache was sized for (4-bit keep 0.25, then 8-bit
+    keep 1): the cache is re-created and rebuilt, and the tokens still equal
+    full-KV decoding."""
+    from draftkv import DraftKVEngine
+    m, _ = device_model("llama_small")
+    prompts = [W.tokens(60, m.vocab_size, seed=s) for s in (31, 32)]
+    eng = DraftKVEngine(m, FixedPolicy(CompressionConfig(4, 0.25), 3), seed=0)
+    sess = eng.session(prompts, 40, 0.0)
+    for _ in range(3):
+        sess.round()
+    small = sess.st.comp
+    eng.controller = FixedPolicy(CompressionConfig(8, 1.0), 3)
+    while not sess.done:
+        sess.round()
+    sess.finish()
+    assert sess.st.comp is not small and sess.st.comp.cb_max > small.cb_max and sess.st.comp.cap > small.cap
+    base = DraftKVEngine(m, seed=0).generate_baseline_batch(prompts, 40, 0.0)
+    for b in range(2):
+        assert sess.results()[b].tokens == base[b]
+
+
 def _tv(a, b):
     return 0.5 * float(np.abs(a - b).sum())
 

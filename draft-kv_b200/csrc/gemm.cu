@@ -28,7 +28,6 @@ constexpr size_t kGemmTickets = 65536;
 uint32_t* device_error_word();
 // tensor-core GEMM (gemm_tc.cu)
 int choose_split_tc(int M, int K);
-
 int gemm_tc(const void* x, const void* w, int M, int N, int K, int S, const EpiArgs& epi, cudaStream_t st);
 int pack_weight_tc(const uint16_t* w, int M, int K, uint16_t* out, cudaStream_t st);
 size_t packed_weight_bytes_tc(int M, int K);

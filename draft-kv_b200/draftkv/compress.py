@@ -242,6 +242,11 @@ class CompressedKVCache:
         self.meta_t.copy_(old[6])
         self.seen_t.copy_(old[7])
 
+    @property
+    def max_bits(self) -> int:
+        """Widest code the slot arrays were sized for (16: raw entries)."""
+        return self._max_bits
+
     def set_cfgs(self, cfgs: Sequence[CompressionConfig]) -> None:
         self.cfgs = list(cfgs)
         self.cfg = self.cfgs[0]

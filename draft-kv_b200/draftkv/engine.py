@@ -299,7 +299,7 @@ class DraftKVEngine:
 
     def _comp_too_small(self, st: _Batch, cfgs) -> bool:
         comp = st.comp
-        return max(c.bits for c in cfgs) > comp._max_bits or self._comp_slots(st, cfgs) > comp.cap
+        return max(c.bits for c in cfgs) > comp.max_bits or self._comp_slots(st, cfgs) > comp.cap
 
     def _rebuild(self, st: _Batch, layers: list, ctx_t, advance: bool) -> None:
         if not layers:

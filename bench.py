@@ -416,8 +416,17 @@ def run_gpu(args) -> None:
     engine.offload_full = bool(conf.get("offload"))
     vocab = model.vocab_size
     prompts = [[int(x) for x in np.random.default_rng(1 + 1000 * rank + b).integers(0, vocab, ctx)] for b in range(B)]
-    sess = engine.session(prompts, max_new, T, exchange=exchange)
     torch.cuda.synchronize()
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record()
+    sess = engine.session(prompts, max_new, T, exchange=exchange)        # the prefill
+    p1.record()
+    torch.cuda.synchronize()
+    prefill = {"tokens": B * (ctx - 1), "seconds": round(p0.elapsed_time(p1) / 1e3, 3),
+               "tokens_per_s": round(B * (ctx - 1) / (p0.elapsed_time(p1) / 1e3), 1),
+               "basis": "engine.session(): chunked full-cache forwards of 512 tokens x the batch, no logits; "
+                        "CUDA events (includes the host's launch of the chunks)"}
     setup_s = time.perf_counter() - t_setup
 
     for _ in range(args.warmup * R):
@@ -725,6 +734,7 @@ def run_gpu(args) -> None:
                 "d2h_bytes_per_step": d2h * R},
         "cpu_baseline": cpu,
         "setup_s": round(setup_s, 1),
+        "prefill": prefill,
     }
     if rank == 0:
         print(json.dumps(line), file=out, flush=True)

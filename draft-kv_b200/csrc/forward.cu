@@ -61,7 +61,7 @@ extern "C" size_t dkv_forward_work_bytes(const dkv_model* m, int batch, int T, i
 
 extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const dkv_comp_cache* comp,
                            const dkv_step* st, void* stream) {
-    DKV_REQUIRE(m && st && m->layers && st->tokens && st->pos0 && st->logits, "dkv_forward: bad arguments");
+    DKV_REQUIRE(m && st && m->layers && st->tokens && st->pos0, "dkv_forward: bad arguments");
     DKV_REQUIRE(comp || (full && full->k_pool && full->page_table),
                 "dkv_forward: a full-cache forward needs the full cache");
     DKV_REQUIRE(m->n_heads % m->n_kv == 0, "dkv_forward: n_heads %% n_kv != 0");
@@ -203,6 +203,7 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
         const dkv_epilogue ed = down_epi(L);
         DKV_TRY(dkv_gemm(act, m->dtype, ly.w_down, m->dtype, round128(dm), N, m->d_ff, &ed, gwork, gemm_bytes, stream));
     }
+    if (!st->logits) return DKV_OK;        // prefill: the cache is written, no logits wanted
     if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, m->nf_w, m->nf_b, m->eps, x, m->dtype, stream));
     const dkv_epilogue eh = head_epi();
     DKV_TRY(dkv_gemm(xin, m->dtype, m->w_head, m->dtype, m->vocab_pad, N, dm, &eh, gwork, gemm_bytes, stream));

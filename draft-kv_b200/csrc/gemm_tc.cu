@@ -101,8 +101,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     cg::cluster_group cluster = cg::this_cluster();
     const int S = g.S;
     const int s = S > 1 ? (int)cluster.block_rank() : 0;
-    const int mtile = blockIdx.x / S;
-    const int nblk = blockIdx.y, n0 = nblk * NB;
+    // one linear grid: split rank fastest (a cluster is one row tile's split
+    // group), then the token block, then the row tile -- the token blocks
+    // of a row tile run together and share its weights through L2
+    const int nblks = (g.N + NB - 1) / NB;
+    const int mtile = (int)(blockIdx.x / S) / nblks;
+    const int nblk = (int)(blockIdx.x / S) % nblks, n0 = nblk * NB;
     const int kb0 = (int)((long long)s * g.KB / S), kb1 = (int)((long long)(s + 1) * g.KB / S);
     const int nstages = (kb1 - kb0 + kTcStageKB - 1) / kTcStageKB;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -421,7 +425,7 @@ cudaError_t tc_launch(const CUtensorMap& map, const TcArgs& g, int mtiles, int n
     cudaError_t e = tc_attrs<NB>();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(mtiles * g.S, nblk);
+    cfg.gridDim = dim3(mtiles * nblk * g.S);
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = TcGeo<NB>::SMEM;
     cfg.stream = st;

@@ -142,6 +142,11 @@ class DraftKVEngine:
         # keep the full cache in pinned host memory after the prefill (the
         # drafter cache stays in HBM); verify streams it over the host link
         self.offload_full = False
+        # prompt tokens per sequence in one prefill forward (prompts of 1024
+        # tokens or more; shorter ones take 64).  Measured on B200, 4 x 32767
+        # tokens of the Llama-3-8B shape: 14.4 s at 256, 13.2 s at 512, 13.1 s
+        # at 1024 (the causal attention over the prompt dominates)
+        self.prefill_chunk = 512
 
         self.full_cache_factory = full_cache_factory
         self.gamma_max = gamma_max
@@ -174,14 +179,13 @@ class DraftKVEngine:
         m, B = self.model, st.B
         lens = [len(p) - 1 for p in prompts]
         L = max(lens) if lens else 0
-        CH = 256 if L >= 1024 else 64        # long prompts: fewer, larger chunks
+        CH = self.prefill_chunk if L >= 1024 else 64        # long prompts: fewer, larger chunks
         tok = torch.zeros((B, max(L, 1)), dtype=torch.int32)
         for b, p in enumerate(prompts):
             if lens[b] > 0:
                 tok[b, :lens[b]] = torch.tensor(p[:-1], dtype=torch.int32)
         tok = tok.to(m.device)
         work = m.work(B, CH, st.full.capacity_tokens, 0)
-        logits = torch.empty((B * CH, m.vocab_size), dtype=torch.float32, device=m.device)
         for b in range(B):
             st.full.ensure(b, lens[b] + st.G + 2)
         for c0 in range(0, L, CH):
@@ -190,7 +194,8 @@ class DraftKVEngine:
             # rows harmlessly; rows past a sequence's prompt are never read
             pos0 = torch.full((B,), c0, dtype=torch.int32, device=m.device)
             tok_c = tok[:, c0:c1].contiguous()
-            m.forward_raw(st.full, None, tok_c.data_ptr(), c1 - c0, pos0, B, c1 - c0, logits, work, CH,
+            # no logits: the reference discards the prompt's (engine.py:133-134)
+            m.forward_raw(st.full, None, tok_c.data_ptr(), c1 - c0, pos0, B, c1 - c0, None, work, CH,
                           st.full.capacity_tokens)
         for b in range(B):
             st.full.set_length(b, lens[b])

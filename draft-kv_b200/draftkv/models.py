@@ -153,15 +153,16 @@ class DeviceDecoder:
     # ------------------------------------------------------------ forward
     def forward_raw(self, full, comp, tokens_ptr: int, tok_stride: int, pos0: "torch.Tensor", batch: int, T: int,
                     logits: "torch.Tensor", work: "torch.Tensor", max_T: int, max_ctx: int) -> None:
-        """One native forward for `batch` sequences x T tokens (device pointers).
+        """One native forward for `batch` sequences x T tokens (device pointers);
+        `logits` None runs no final norm and head (a prefill chunk).
 
         With `use_graphs` a forward whose arguments (every address, size and
         the drafter's per-layer configs) have been seen before is replayed as a
         CUDA graph: the second call with given arguments captures it, later
         calls replay it.  The token, position and cache contents are read at
         replay time; only the launch parameters are frozen."""
-        step = _lib.StepS(batch, T, tokens_ptr, tok_stride, pos0.data_ptr(), logits.data_ptr(), work.data_ptr(),
-                          work.numel(), max_ctx, max_T)
+        step = _lib.StepS(batch, T, tokens_ptr, tok_stride, pos0.data_ptr(), None if logits is None else logits.data_ptr(),
+                          work.data_ptr(), work.numel(), max_ctx, max_T)
         fs = None if full is None else full.struct()        # (syncs a changed page table first)
         cs = None if comp is None else comp.struct()
 

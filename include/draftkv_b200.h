@@ -375,7 +375,9 @@ typedef struct {
     const int32_t* tokens;        /* token (b,t) = tokens[b*tok_stride + t] */
     int tok_stride;
     const int32_t* pos0;          /* [batch] position of token t=0 */
-    float* logits;                /* [batch*T][vocab_pad] f32 */
+    float* logits;                /* [batch*T][vocab_pad] f32, or NULL: no final norm and head
+                                     (a prefill that only writes the cache; the reference discards
+                                     those logits, draftkv/engine.py:133-134) */
     /* scratch (caller allocates dkv_forward_work_bytes) */
     void* work;
     size_t work_bytes;

@@ -999,6 +999,8 @@ def run_kernel(args) -> None:
         p0 = torch.full((B,), ctx - T, dtype=torch.int32, device="cuda")
         outv = torch.zeros((B * T, n_kv * G * d), dtype=torch.bfloat16, device="cuda")
         by = B * n_kv * ctx * 2 * d * 2
+        # causal: query t (position ctx - T + t) sees ctx - T + t + 1 keys; 4 flops a (key, dim) pair
+        line["flops"] = B * n_kv * G * sum(ctx - T + t + 1 for t in range(T)) * d * 4
         us = timeit(lambda: _lib.call("dkv_attn_full", full.struct(), full.dims(), 0, G, T, qv.data_ptr(),
                                       p0.data_ptr(), outv.data_ptr(), _lib.BF16, args.split, work.data_ptr(), work.numel(),
                                       _lib.stream_ptr()))
@@ -1069,6 +1071,10 @@ def run_kernel(args) -> None:
                                       C.byref(e), work.data_ptr(), work.numel(), _lib.stream_ptr()))
         line["config"] = {"M": M, "K": K, "N": N}
     gbs = by / (us * 1e-6) / 1e9
+    if "flops" in line:
+        tf = line["flops"] / (us * 1e-6) / 1e12
+        line.update({"achieved_tflops": round(tf, 1), "peak_tflops": round(pk["bf16_tflops"], 1),
+                     "tensor_frac": round(tf / pk["bf16_tflops"], 4)})
     line.update({"us": round(us, 2), "algorithmic_bytes": int(by), "achieved_gbs": round(gbs, 1),
                  "peak_gbs": round(pk["hbm_gbs"], 1), "frac": round(gbs / pk["hbm_gbs"], 4),
                  "peak_source": pk["source"],

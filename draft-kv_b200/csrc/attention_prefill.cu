@@ -1,0 +1,466 @@
+// Prefill attention on the fifth-generation tensor cores: a chunk's query
+// rows attend causally to the paged full cache (bf16, 16-key pages in device
+// memory).  Replaces the attention of the prompt forward (draftkv/engine.py:
+// 133-134 running draftkv/llama.py:202-219 over every prompt position).
+//
+// One CTA per (sequence, KV head, key split, block of 128 query rows), rows =
+// token x GQA head as in the other attention kernels; 6 warps:
+//   warp 4 -- producer: per 128-key tile, one copy of 128 keys x 64 dims
+//     when the tile's 8 pages are consecutive in the pool (ascending, or
+//     descending for a tile no row masks), else 8 lanes issue one page each
+//     (16 keys x 64 dims, 2 KB; one copy engine serves the SM at ~90 cycles a
+//     2 KB box, so fewer, larger boxes are faster); 128-byte swizzle, 3-deep
+//     K and V rings; pages wholly past the CTA's last key are read past the
+//     pool view (zeros).  K_j is copied once S_{j-3} has read its slot, V_{j-1} once
+//     P_{j-4} V_{j-4} has;
+//   warp 5 -- TMEM allocation; lane 0 issues the MMAs: S_j = Q K_j^T into
+//     one of two 128-column TMEM buffers (M 128 rows, N 128 keys, K = d; Q in
+//     TMEM), then O += P_{j-1} V_{j-1} (M 128, N d, K 128 keys; P in TMEM
+//     where S_{j-1} was, V read in place through an MN-major descriptor), so
+//     the tensor core computes the next scores while the softmax works;
+//   warps 0-3 -- softmax, one query row a thread (TMEM lane = row): first
+//     the row of Q (bf16) into TMEM, then per tile the row's 128 scores
+//     (tcgen05.ld), causal mask, running max, exp2, and bf16 P back into TMEM
+//     over the scores.  O is rescaled in TMEM only when the row max grows by
+//     more than 8 (log2 units): a stale max leaves O / l exact and keeps
+//     every P below 2^8.
+// The tensor core reads only K and V from shared memory (Q and P stay in
+// tensor memory): at 128 B/clock a tile's copies in and MMA reads out take
+// about as long as its MMAs.  MMAs execute in issue order, so S_{j+2} (issued
+// after P_j V_j) cannot overwrite P_j before it is read.
+// At the end the O rows (tcgen05.ld) go to the split partials, merged in
+// split order as in the other attention kernels.  Scores are in log2 units
+// (log2 e folded into the query scale).  Every mbarrier wait is bounded
+// (error word 0x80); after a failed wait the CTA waits (bounded) for its
+// copies and MMAs in flight before it frees shared and tensor memory.
+#include "attn_common.cuh"
+#include "tcgen05.cuh"
+
+namespace dkv {
+
+uint32_t* device_error_word();
+
+constexpr int kPfRows = 128;          // query rows per CTA (MMA M, TMEM lanes)
+constexpr int kPfKeys = 128;          // keys per tile
+constexpr int kPfThreads = 192;       // 4 softmax warps, producer, MMA
+constexpr int kPfNst = 3;             // K and V ring depth
+constexpr int kPfTmemCols = 512;
+constexpr int kPfColO = 256;          // TMEM columns: S0 0-127 (P0 0-63), S1 128-255, O 256+, Q 384+
+constexpr int kPfColQ = 384;
+constexpr int kPfSplitPages = 1024;   // page ids staged in shared memory
+constexpr float kPfRescale = 8.f;     // lazy-rescale threshold (log2 units)
+
+// Shared memory (from a 1024-byte aligned base): K slots [3][d/64][128 keys]
+// [64] then V slots (same arrangement), every 128 x 64 block in the 128-byte
+// swizzle (row r at r * 128 bytes, its 16-byte unit u at u ^ (r % 8)).
+template <int D>
+struct PfGeo {
+    static constexpr int CH = D / 64;
+    static constexpr int KVB = CH * 16384;       // one K (or V) tile
+    static constexpr int V0 = kPfNst * KVB;      // first V slot
+    static constexpr size_t SMEM = (size_t)2 * kPfNst * KVB + 1024;
+};
+
+DKV_DEV uint32_t pf_pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+DKV_DEV float pf_ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    return y;
+}
+DKV_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// D (TMEM) += A (TMEM: row i in lane i, two bf16 a 32-bit column) . B (shared)
+DKV_DEV void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __grid_constant__ KvMaps maps, AttnArgs a) {
+    using Geo = PfGeo<D>;
+    constexpr int PS = D + 2;
+    constexpr float kLog2e = 1.4426950408889634f, kLn2 = 0.6931471805599453f;
+    extern __shared__ uint8_t pf_raw[];
+    uint8_t* sm = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);
+    __shared__ __align__(8) uint64_t k_full[kPfNst], k_empty[kPfNst], v_full[kPfNst], v_empty[kPfNst];
+    __shared__ __align__(8) uint64_t s_full[2], p_full, o_done, drain;
+    __shared__ uint32_t tmem_slot;
+    __shared__ float ms[kPfRows], ls[kPfRows];
+    __shared__ int32_t pages_s[kPfSplitPages];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // one linear grid, row block fastest: the row blocks of a (sequence,
+    // head, split) run together and read each K/V tile through L2
+    const int rb = (int)(blockIdx.x % a.n_rb);
+    const int s = (int)(blockIdx.x / a.n_rb % a.n_splits);
+    const int h = (int)(blockIdx.x / a.n_rb / a.n_splits % a.n_kv);
+    const int b = (int)(blockIdx.x / a.n_rb / a.n_splits / a.n_kv);
+    const int G = a.group, T = a.T;
+    const int r0 = rb * kPfRows;
+    const int R = min(kPfRows, T * G - r0);
+    const int HQ = a.n_kv * G;
+    const size_t bhr = ((size_t)b * a.n_kv + h) * a.n_rb + rb;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPfNst; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+        }
+        mbar_init(&s_full[0], 1);
+        mbar_init(&s_full[1], 1);
+        mbar_init(&p_full, 128);
+        mbar_init(&o_done, 1);
+        mbar_init(&drain, 1);
+        fence_barrier_init();
+        fence_async_shared();
+    }
+    if (warp == 5) tmem_alloc(&tmem_slot, kPfTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    pdl_trigger();
+    pdl_wait();      // the queries and the chunk's cache rows come from earlier kernels
+
+    const int qbase = a.qpos0[b];
+    const int n_keys = qbase + T;
+    const int k0 = s * a.split;                         // a multiple of 128
+    const int tmax = (r0 + R - 1) / G;                  // this CTA's last token
+    const int kend = min(min(n_keys, k0 + a.split), qbase + tmax + 1);
+    const int ntiles = kend > k0 ? (kend - k0 + kPfKeys - 1) / kPfKeys : 0;
+    const int32_t* ptab = a.src.page_table + ((size_t)b * a.n_layers + a.layer) * a.src.max_pages;
+    const int npg = kend > k0 ? (kend - k0 + 15) / 16 : 0;
+    const bool staged = npg <= kPfSplitPages;
+
+    bool ok = true;
+    int issued_k = 0, issued_v = 0;    // producer: tiles whose K / V copies were issued
+    if (warp == 4) {
+        // ---------------- producer: the split's page ids, then per tile j the
+        // copies of K_j and of V_{j-1}; lane p issues page p's boxes (one
+        // lane's copies issue ~125 cycles apart), lane 0 arms the barrier
+        if (staged) {
+            for (int i = lane; i < npg; i += 32) pages_s[i] = __ldg(ptab + (k0 >> 4) + i);
+            __syncwarp();
+        }
+        const bool live = lane < kPfKeys / 16;
+        // keys below kfree are live for every row of the CTA (no mask)
+        const int kfree = min(qbase + r0 / G + 1, kend);
+        auto issue = [&](int j, bool v) {
+            const int slot = j % kPfNst;
+            uint8_t* dst = sm + (v ? Geo::V0 : 0) + slot * Geo::KVB;
+            uint64_t* bar = v ? &v_full[slot] : &k_full[slot];
+            if (lane == 0) mbar_expect_tx(bar, (uint32_t)Geo::KVB);
+            __syncwarp();
+            const int key = k0 + j * kPfKeys + 16 * lane;
+            const int page = live ? (key < kend ? (staged ? pages_s[(key - k0) >> 4] : __ldg(ptab + (key >> 4)))
+                                                : a.src.n_pages)
+                                  : 0;
+            const int first = __shfl_sync(0xffffffffu, page, 0);
+            const bool unmasked = k0 + (j + 1) * kPfKeys <= kfree;
+            if (__all_sync(0xffffffffu, !live || page == first + lane)) {
+                // the tile's 8 pages are consecutive in the pool: one copy of
+                // 128 keys per 64 dims (pages past the pool read zeros)
+                if (lane == 0)
+#pragma unroll
+                    for (int x = 0; x < Geo::CH; ++x)
+                        tma_load_4d(dst + x * 16384, v ? &maps.v8 : &maps.k8, x * 64, 0, h, first, bar);
+            } else if (unmasked && __all_sync(0xffffffffu, !live || page == first - lane)) {
+                // consecutive in descending order (the block pool hands out
+                // its free list last-in first-out): one copy from the lowest
+                // page puts the 16-key blocks in reverse order.  K and V get
+                // the same order, so S, P and V stay consistent, and the max
+                // and sum do not depend on order: only for tiles no row masks
+                if (lane == 0)
+#pragma unroll
+                    for (int x = 0; x < Geo::CH; ++x)
+                        tma_load_4d(dst + x * 16384, v ? &maps.v8 : &maps.k8, x * 64, 0, h, first - 7, bar);
+            } else if (live) {
+#pragma unroll
+                for (int x = 0; x < Geo::CH; ++x)
+                    tma_load_4d(dst + x * 16384 + lane * 2048, v ? &maps.v : &maps.k, x * 64, 0, h, page, bar);
+            }
+        };
+        for (int j = 0; j <= ntiles; ++j) {
+            if (j < ntiles) {
+                // slot j % 3 was last read by S_{j-3}
+                if (j >= kPfNst && !__all_sync(0xffffffffu, mbar_wait(&k_empty[j % kPfNst],
+                                                                      (uint32_t)((j / kPfNst - 1) & 1), a.err))) {
+                    ok = false;
+                    break;
+                }
+                issue(j, false);
+                issued_k = j + 1;
+            }
+            if (j >= 1) {
+                const int i = j - 1;     // slot i % 3 was last read by P_{i-3} V_{i-3}
+                if (i >= kPfNst && !__all_sync(0xffffffffu, mbar_wait(&v_empty[i % kPfNst],
+                                                                      (uint32_t)((i / kPfNst - 1) & 1), a.err))) {
+                    ok = false;
+                    break;
+                }
+                issue(i, true);
+                issued_v = i + 1;
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer (the warp waits together, lane 0 issues)
+        const uint32_t ring_s = smem_u32(sm);
+        constexpr uint32_t idS = tc_idesc_n(kPfKeys, false), idO = tc_idesc_n(D, true);
+        auto issue_pv = [&](int i) -> bool {
+            const int slot = i % kPfNst;
+            if (!__all_sync(0xffffffffu, mbar_wait(&p_full, (uint32_t)(i & 1), a.err))) return false;
+            if (!__all_sync(0xffffffffu, mbar_wait(&v_full[slot], (uint32_t)((i / kPfNst) & 1), a.err)))
+                return false;
+            const int t0 = k0 + i * kPfKeys;
+            if (kend - t0 < kPfKeys && (kend & 15) != 0) {
+                // the rest of the last page holds whatever the pool held
+                // there: zero those V rows (their P is 0, but 0 x NaN is not)
+                uint8_t* vd = sm + Geo::V0 + slot * Geo::KVB;
+                const int z0 = kend - t0, z1 = (z0 + 15) & ~15;
+                for (int e = lane; e < (z1 - z0) * (D / 8); e += 32) {
+                    const int key = z0 + e / (D / 8), u = e % (D / 8);
+                    *reinterpret_cast<uint4*>(vd + (u >> 3) * 16384 + key * 128 + (((u & 7) ^ (key & 7)) << 4)) =
+                        make_uint4(0u, 0u, 0u, 0u);
+                }
+                fence_async_shared();
+                __syncwarp();
+            }
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t v_s = ring_s + Geo::V0 + slot * Geo::KVB;
+                const uint32_t p_t = tmem + (uint32_t)((i & 1) * kPfKeys);
+#pragma unroll
+                for (int ks = 0; ks < kPfKeys / 16; ++ks)
+                    tc_mma_ts(tmem + kPfColO, p_t + ks * 8, sw128_desc_mn(v_s + ks * 2048, 16384), idO,
+                              (i | ks) != 0 ? 1u : 0u);
+                tc_commit(&o_done);
+                tc_commit(&v_empty[slot]);
+            }
+            __syncwarp();
+            return true;
+        };
+        named_sync(1, 160);      // Q is in TMEM
+        tc_fence_after();
+        for (int j = 0; j < ntiles; ++j) {
+            const int slot = j % kPfNst;
+            if (!__all_sync(0xffffffffu, mbar_wait(&k_full[slot], (uint32_t)((j / kPfNst) & 1), a.err))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+                // S buffer j % 2 last held P_{j-2}: P_{j-2} V_{j-2} was issued
+                // before this (in-order execution)
+                const uint32_t k_s = ring_s + slot * Geo::KVB;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    tc_mma_ts(tmem + (uint32_t)((j & 1) * kPfKeys), tmem + kPfColQ + kk * 8,
+                              sw128_desc(k_s + (kk >> 2) * 16384 + (kk & 3) * 32), idS, kk != 0 ? 1u : 0u);
+                tc_commit(&s_full[j & 1]);
+                tc_commit(&k_empty[slot]);
+            }
+            __syncwarp();
+            if (j >= 1 && !issue_pv(j - 1)) {
+                ok = false;
+                break;
+            }
+        }
+        if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
+    } else {
+        // ---------------- softmax: row r = threadIdx.x (TMEM lane r)
+        const int r = threadIdx.x;
+        const uint32_t lanes = tmem + ((uint32_t)(warp * 32) << 16);
+        {
+            // the row of Q: bf16 of q * scale * log2 e, two a column; rows >= R zero
+            const float sc = a.scale * kLog2e;
+            const float* qrow =
+                r < R ? a.q + (((size_t)b * T + (r0 + r) / G) * HQ + h * G + (r0 + r) % G) * D : nullptr;
+#pragma unroll
+            for (int c0 = 0; c0 < D / 2; c0 += 32) {
+                uint32_t qv[32];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (qrow) x = __ldg(reinterpret_cast<const float4*>(qrow + 2 * (c0 + e)));
+                    qv[e] = pf_pack(x.x * sc, x.y * sc);
+                    qv[e + 1] = pf_pack(x.z * sc, x.w * sc);
+                }
+                tmem_st32(lanes + kPfColQ + c0, qv);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            named_sync(1, 160);      // with the MMA warp
+        }
+        const int qp = r < R ? qbase + (r0 + r) / G : kend - 1;     // padding rows see every key
+        const int lim = min(qp, kend - 1);                          // this row's last key
+        float m = -INFINITY, l = 0.f;
+        for (int j = 0; j < ntiles; ++j) {
+            const uint32_t sb = lanes + (uint32_t)((j & 1) * kPfKeys);
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (uint32_t)((j >> 1) & 1), a.err))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(sb + c * 32, sr[c]);
+            tmem_wait_ld();
+            const int lc = lim - (k0 + j * kPfKeys);                  // last live column
+            if (lc < kPfKeys - 1) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (c * 32 + e > lc) sr[c][e] = __float_as_uint(-INFINITY);
+            }
+            float mx[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                mx[c] = __uint_as_float(sr[c][0]);
+#pragma unroll
+                for (int e = 1; e < 32; ++e) mx[c] = fmaxf(mx[c], __uint_as_float(sr[c][e]));
+            }
+            const float mn = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+            float alpha = 1.f;
+            if (m == -INFINITY || mn > m + kPfRescale) {
+                alpha = m == -INFINITY ? 0.f : pf_ex2(m - mn);
+                m = mn;
+            }
+            const float msub = m == -INFINITY ? 0.f : m;
+            float sum[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[2][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const float p0 = pf_ex2(__uint_as_float(sr[c][e]) - msub);
+                    const float p1 = pf_ex2(__uint_as_float(sr[c][e + 1]) - msub);
+                    sum[c] += p0 + p1;
+                    pk[c >> 1][(c & 1) * 16 + e / 2] = pf_pack(p0, p1);
+                }
+            l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+            if (j >= 1) {
+                // P_{j-1} V_{j-1} has updated O (the waits stay in phase order)
+                if (!__all_sync(0xffffffffu, mbar_wait(&o_done, (uint32_t)((j - 1) & 1), a.err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+                    for (int c0 = 0; c0 < D; c0 += 32) {
+                        uint32_t o[32];
+                        tmem_ld32(lanes + kPfColO + c0, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st32(lanes + kPfColO + c0, o);
+                    }
+                }
+            }
+            // P_j over the first 64 columns of S_j
+            tmem_st32(sb, pk[0]);
+            tmem_st32(sb + 32, pk[1]);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full);
+        }
+        if (ok && ntiles > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&o_done, (uint32_t)((ntiles - 1) & 1), a.err));
+            tc_fence_after();
+        }
+        // ---- this split's partial row: (max in natural units, sum, O)
+        float* mypart = a.part + ((bhr * a.n_splits + s) * kPfRows + r) * PS;
+        const bool live = ok && ntiles > 0 && m != -INFINITY;
+        if (__all_sync(0xffffffffu, ok) && ntiles > 0) {
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 32) {
+                uint32_t o[32];
+                tmem_ld32(lanes + kPfColO + c0, o);
+                tmem_wait_ld();
+                if (live && r < R) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2)
+                        *reinterpret_cast<float2*>(mypart + 2 + c0 + e) =
+                            make_float2(__uint_as_float(o[e]), __uint_as_float(o[e + 1]));
+                }
+            }
+        }
+        if (r < R) {
+            mypart[0] = live ? m * kLn2 : -INFINITY;
+            mypart[1] = live ? l : 0.f;
+        }
+    }
+
+    // ---- teardown: one verdict for the CTA; after a failure wait (bounded)
+    // for the copies and MMAs still in flight
+    const bool all_ok = __syncthreads_and(ok) != 0;
+    if (!all_ok) {
+        if (warp == 4 && lane == 0) {
+            for (int j = max(0, issued_k - kPfNst); j < issued_k; ++j)
+                mbar_wait(&k_full[j % kPfNst], (uint32_t)((j / kPfNst) & 1), nullptr);
+            for (int j = max(0, issued_v - kPfNst); j < issued_v; ++j)
+                mbar_wait(&v_full[j % kPfNst], (uint32_t)((j / kPfNst) & 1), nullptr);
+        }
+        if (warp == 5 && lane == 0) {
+            tc_commit(&drain);     // arrives once every MMA issued so far has completed
+            mbar_wait(&drain, 0u, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kPfTmemCols);
+    }
+    // after a failure (error word set) every row of this split is empty, and
+    // the merge still runs so that the tickets stay consistent
+    split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls);
+}
+
+// Host: the prefill launch of dkv_attn_full (rows > 64, bf16 pool in device
+// memory with 16-key pages, d 64 or 128, 16-byte aligned queries).  Splits
+// of the key range are a multiple of 128 keys (the caller's split rounded
+// up); partials and tickets come from the attention work buffer.
+int attn_prefill_tc(AttnArgs& a, dkv_dims dims, const KvMaps& maps, void* work, size_t work_bytes, int max_keys,
+                    cudaStream_t st) {
+    const int R = a.T * a.group;
+    a.split = (a.split + kPfKeys - 1) / kPfKeys * kPfKeys;
+    a.n_rb = (R + kPfRows - 1) / kPfRows;
+    a.n_splits = std::max(1, (max_keys + a.split - 1) / a.split);
+    const size_t n_tk = (size_t)dims.batch * dims.n_kv * a.n_rb;
+    constexpr size_t kTickets = 16384;     // the fixed ticket region at the start of the work buffer
+    DKV_REQUIRE(n_tk + dims.batch <= kTickets, "attention: batch x heads x row blocks too large");
+    Arena ar(work, work_bytes);
+    a.tickets = ar.take<unsigned>(kTickets);
+    a.fold_tickets = a.tickets ? a.tickets + n_tk : nullptr;
+    a.part = ar.take<float>(n_tk * a.n_splits * kPfRows * (dims.d + 2));
+    a.sbuf = nullptr;
+    a.err = device_error_word();
+    DKV_REQUIRE(a.part && a.tickets, "attention: work buffer too small (%zu bytes)", work_bytes);
+    dim3 grid((unsigned)(n_tk * a.n_splits));
+    ProfScope ps(DKV_PROF_ATTN_FULL, 0.0, st);
+    cudaError_t e;
+    if (dims.d == 128) {
+        e = allow_smem_max_once<attn_prefill_tc_kernel<128>>();
+        if (e == cudaSuccess)
+            e = launch_pdl(attn_prefill_tc_kernel<128>, grid, dim3(kPfThreads), PfGeo<128>::SMEM, st, maps, a);
+    } else {
+        e = allow_smem_max_once<attn_prefill_tc_kernel<64>>();
+        if (e == cudaSuccess)
+            e = launch_pdl(attn_prefill_tc_kernel<64>, grid, dim3(kPfThreads), PfGeo<64>::SMEM, st, maps, a);
+    }
+    DKV_CUDA(e);
+    return DKV_OK;
+}
+
+}  // namespace dkv

@@ -314,13 +314,6 @@ DKV_DEV uint32_t movm_trans(uint32_t x) {
     return y;
 }
 
-// Tensor maps of the K and V pools for the TMA-fed kernel: 4-D views
-// {d, 16 page rows, n_kv, n_pages} with a box of {64, 16, 1, 1} (one page's
-// 16 keys of one head, 64 dims) and 128-byte swizzle.
-struct KvMaps {
-    CUtensorMap k, v;
-};
-
 // Element offset of (key, 16-byte chunk) in a 64-key K or V tile.  TMA
 // tiles: [d/64 halves][64 keys][64 dims], 128-byte rows with the chunk XOR
 // (key % 8) that the copy engine's swizzle writes; cp.async tiles: [64][d]
@@ -331,14 +324,6 @@ DKV_DEV int kv_off(int key, int chunk) {
         return (chunk >> 3) * (kTcKT * 64) + key * 64 + (((chunk & 7) ^ (key & 7)) << 3);
     else
         return swz<D>(key, chunk);
-}
-
-DKV_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-        "[%6];\n" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
-        : "memory");
 }
 
 template <int D, int MAXT, bool TMA>
@@ -648,8 +633,11 @@ bool kv_maps(const KeySrc& src, int n_kv, int d, KvMaps* out) {
         const uint64_t dims[4] = {(uint64_t)d, 16, (uint64_t)n_kv, (uint64_t)src.n_pages};
         const uint64_t strides[3] = {(uint64_t)d * 2, (uint64_t)16 * d * 2, (uint64_t)16 * d * 2 * n_kv};
         const uint32_t box[4] = {64, 16, 1, 1};
+        const uint32_t box8[4] = {64, 16, 1, 8};
         e.ok = encode_bf16_map(&e.maps.k, src.k_pool, 4, dims, strides, box) == DKV_OK &&
-               encode_bf16_map(&e.maps.v, src.v_pool, 4, dims, strides, box) == DKV_OK;
+               encode_bf16_map(&e.maps.v, src.v_pool, 4, dims, strides, box) == DKV_OK &&
+               encode_bf16_map(&e.maps.k8, src.k_pool, 4, dims, strides, box8) == DKV_OK &&
+               encode_bf16_map(&e.maps.v8, src.v_pool, 4, dims, strides, box8) == DKV_OK;
     }
     cache[next] = e;
     next = (next + 1) % 32;
@@ -660,6 +648,8 @@ bool kv_maps(const KeySrc& src, int n_kv, int d, KvMaps* out) {
 
 int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int max_keys, cudaStream_t st,
                  bool* handled);
+int attn_prefill_tc(AttnArgs& a, dkv_dims dims, const KvMaps& maps, void* work, size_t work_bytes, int max_keys,
+                    cudaStream_t st);
 int attn_comp_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, cudaStream_t st, bool* handled);
 
 constexpr size_t kAttnTicketsTc = 16384;   // same fixed ticket region as the generic kernel
@@ -670,6 +660,15 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
     if (a.src.dtype != DKV_BF16 || (dims.d != 64 && dims.d != 128) || a.split % kTcKT != 0) return DKV_OK;
     if (a.src.page_shift < 0) return DKV_OK;     // pages of any other size: generic kernel
     const int R = a.T * a.group;
+    if (R > kAttnRB && ((uintptr_t)a.q & 15) == 0) {
+        // prefill chunks over a device-resident pool: the tcgen05 kernel
+        KvMaps pm;
+        if (kv_maps(a.src, dims.n_kv, dims.d, &pm)) {
+            DKV_TRY(attn_prefill_tc(a, dims, pm, work, work_bytes, max_keys, st));
+            *handled = true;
+            return DKV_OK;
+        }
+    }
     a.n_rb = R <= kAttnRB ? (R + kKqRows - 1) / kKqRows : (R + kAttnRB - 1) / kAttnRB;
     a.n_splits = (max_keys + a.split - 1) / a.split;
     if (a.n_splits < 1) a.n_splits = 1;

@@ -1,6 +1,8 @@
 // Arguments and the split merge shared by the attention kernels.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace dkv {
@@ -48,12 +50,35 @@ struct AttnArgs {
 
 constexpr int kAttnRB = 64;   // query rows (token x group head) per CTA
 
+// Tensor maps of the K and V pools for the copy-engine-fed kernels: 4-D views
+// {d, 16 page rows, n_kv, n_pages} with 128-byte swizzle; k / v copy a box of
+// {64, 16, 1, 1} (one page's 16 keys of one head, 64 dims), k8 / v8 a box of
+// {64, 16, 1, 8} (8 consecutive pages: 128 keys in one copy).
+struct KvMaps {
+    CUtensorMap k, v, k8, v8;
+};
+// The cached maps of a device-resident pool with 16-row pages; false when the
+// pool is elsewhere (pinned host memory) or has pages of another size.
+bool kv_maps(const KeySrc& src, int n_kv, int d, KvMaps* out);
+
+// One box of a 4-D tensor map into this CTA's shared memory (no multicast),
+// completing on `bar`.  Coordinates past the view's bounds read zeros.
+DKV_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];\n" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // After a CTA has stored its partial rows (m, l, unnormalised O) for split s
 // of (sequence, head, row block) `bhr`, the last CTA to arrive merges every
 // split in split order (splits with no live key skipped), writes the output
 // rows and returns true with the merged max / sum in ms / ls (R rows).
 // The merge order is fixed, so a row's result is the same whatever the number
-// of rows or splits that share the launch.
+// of rows or splits that share the launch.  RB: the row stride of a split's
+// partial block (the launch's rows per CTA).
+template <int RB = kAttnRB>
 DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int r0, float* ms, float* ls) {
     const int d = a.d, G = a.group, T = a.T, PS = d + 2, HQ = a.n_kv * G;
     __threadfence();
@@ -68,15 +93,15 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
     __syncthreads();
     if (!is_last) return false;
     __threadfence();
-    const float* parts = a.part + (bhr * a.n_splits) * kAttnRB * PS;
+    const float* parts = a.part + (bhr * a.n_splits) * RB * PS;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float M = -INFINITY;
-        for (int q = 0; q < a.n_splits; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * kAttnRB + r) * PS));
+        for (int q = 0; q < a.n_splits; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * RB + r) * PS));
         float L = 0.f;
         for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * kAttnRB + r) * PS);
+            const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
             if (mq == -INFINITY) continue;
-            L += __ldcg(parts + ((size_t)q * kAttnRB + r) * PS + 1) * expf(mq - M);
+            L += __ldcg(parts + ((size_t)q * RB + r) * PS + 1) * expf(mq - M);
         }
         ms[r] = M;
         ls[r] = L;
@@ -87,9 +112,9 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
         const float M = ms[r];
         float acc = 0.f;
         for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * kAttnRB + r) * PS);
+            const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
             if (mq == -INFINITY) continue;
-            acc += __ldcg(parts + ((size_t)q * kAttnRB + r) * PS + 2 + e) * expf(mq - M);
+            acc += __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) * expf(mq - M);
         }
         const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
         const int t = (r0 + r) / G, g = (r0 + r) % G;

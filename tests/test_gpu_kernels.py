@@ -522,6 +522,55 @@ def test_full_attention_matches_torch_and_decode(dtype, G, d):
         assert torch.equal(o1[0], out[t]), t
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("G", [1, 4])
+@pytest.mark.parametrize("n,T,split", [(700, 700, 3648), (1000, 37, 256), (4100, 300, 1024)])
+def test_prefill_attention_matches_torch(d, G, n, T, split):
+    """The tcgen05 prefill kernel (more than 64 query rows, bf16 pool in
+    device memory): causal GQA attention of T new tokens at positions
+    n-T..n-1 against a float64 reference, at most 2e-2 per element and 1e-3
+    on average.  q * scale * log2 e and p are bf16 operands: in these cases
+    that rounding alone (modelled in float64 with the kernel's 128-key tiles,
+    splits and lazy rescale) moves single outputs by up to 1.24e-2 and the
+    mean by 2.5e-4 to 5.8e-4.  Cases: a whole 700-token prompt (ragged last
+    row block, one split), 37 tokens over 1000 keys in 256-key splits (rows
+    whose split starts past their position), 300 tokens over 4100 keys;
+    every context ends inside a page whose unused rows hold NaN."""
+    from draftkv import PagedKVCache
+    L = lib()
+    n_kv = 2
+    cache = PagedKVCache(1, n_kv, d, 16, (n + 15) // 16 + 4, "bf16", batch=1)
+    cache.k_pool.fill_(float("nan"))
+    cache.v_pool.fill_(float("nan"))
+    rng = np.random.default_rng(n + G + d)
+    k = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    v = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
+    cache.append(0, k, v, np.arange(n))
+    p0 = n - T
+    q = torch.from_numpy(rng.standard_normal((T, n_kv * G, d)).astype(np.float32) * 2).cuda()
+    pos0 = torch.tensor([p0], dtype=torch.int32, device="cuda")
+    dims = cache.dims()
+    work = torch.zeros(int(L.load().dkv_attn_work_bytes(dims, G, T, cache.capacity_tokens, split, 0)),
+                       dtype=torch.uint8, device="cuda")
+    out = torch.zeros((T, n_kv * G * d), dtype=torch.float32, device="cuda")
+    kk = torch.from_numpy(k).cuda().repeat_interleave(G, dim=1).double()
+    vv = torch.from_numpy(v).cuda().repeat_interleave(G, dim=1).double()
+    mask = torch.arange(n, device="cuda")[None, :] > (p0 + torch.arange(T, device="cuda"))[:, None]
+    s = torch.einsum("qhd,khd->qhk", q.double(), kk) / np.sqrt(d)
+    s = s.masked_fill(mask[:, None, :], float("-inf"))
+    ref = torch.einsum("qhk,khd->qhd", torch.softmax(s, -1), vv).reshape(T, -1).float()
+    for _ in range(2):       # the second launch reuses the tickets the first one reset
+        out.zero_()
+        L.call("dkv_attn_full", cache.struct(), dims, 0, G, T, q.data_ptr(), pos0.data_ptr(), out.data_ptr(), L.F32,
+               split, work.data_ptr(), work.numel(), L.stream_ptr())
+        assert torch.isfinite(out).all()
+        torch.testing.assert_close(out, ref, rtol=2e-2, atol=2e-2)
+        assert (out - ref).abs().mean().item() <= 1e-3
+    code = C.c_uint32(0)
+    L.call("dkv_device_error", C.byref(code), L.stream_ptr())
+    assert code.value == 0
+
+
 def test_drafter_capacity_is_whole_tiles():
     """The tensor-core drafter kernel copies 16-slot tiles: every capacity the
     cache allocates (initial and grown) is a multiple of 16."""

@@ -12,6 +12,8 @@ namespace dkv {
 size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap, size_t* attn_bytes,
                     size_t* gemm_bytes);
 int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st);
+int gemm_entry(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K, const dkv_epilogue* epi,
+               void* work, size_t work_bytes, void* stream, bool fill);
 
 // RMSNorm fused into the GEMMs (bf16 Llama-family models): the norm before
 // the QKV, gate/up and head projections costs no launch of its own.
@@ -179,6 +181,12 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
         return e;
     };
 
+    // the prompt forward (no logits): its rows feed only the cache, so each
+    // projection takes the K split that fills the GPU for this many tokens
+    const bool prompt = st->logits == nullptr;
+    auto gemm = [&](const void* xa, const void* w, int M, int K, const dkv_epilogue* e) {
+        return dkv::gemm_entry(xa, m->dtype, w, m->dtype, M, N, K, e, gwork, gemm_bytes, stream, prompt);
+    };
     DKV_TRY(dkv_embed(m->tok_emb, m->dtype, m->pos_emb, st->tokens, st->tok_stride, st->batch, st->T, st->pos0, dm,
                       m->vocab, m->max_pos, h, stream));
     if (fused) DKV_TRY(norm_prep(h, N, dm, m->layers[0].n1_w, xn, npart, (int)NM, (cudaStream_t)stream));
@@ -186,7 +194,7 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
         const dkv_layer& ly = m->layers[L];
         if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n1_w, ly.n1_b, m->eps, x, m->dtype, stream));
         const dkv_epilogue e = qkv_epi(L);
-        DKV_TRY(dkv_gemm(xin, m->dtype, ly.w_qkv, m->dtype, M_qkv, N, dm, &e, gwork, gemm_bytes, stream));
+        DKV_TRY(gemm(xin, ly.w_qkv, M_qkv, dm, &e));
         if (comp) {
             DKV_TRY(dkv_comp_append(comp, full, dims, L, 1, stage, m->dtype, 1, st->pos0, nullptr, nullptr, L == 0 ? 1 : 0,
                                     stream));
@@ -196,12 +204,12 @@ extern "C" int dkv_forward(const dkv_model* m, const dkv_full_cache* full, const
                                   attn_bytes, stream));
         }
         const dkv_epilogue eo = o_epi(L);
-        DKV_TRY(dkv_gemm(x, m->dtype, ly.w_o, m->dtype, round128(dm), N, HD, &eo, gwork, gemm_bytes, stream));
+        DKV_TRY(gemm(x, ly.w_o, round128(dm), HD, &eo));
         if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, ly.n2_w, ly.n2_b, m->eps, x, m->dtype, stream));
         const dkv_epilogue eu = up_epi(L);
-        DKV_TRY(dkv_gemm(xin, m->dtype, ly.w_up, m->dtype, M_up, N, dm, &eu, gwork, gemm_bytes, stream));
+        DKV_TRY(gemm(xin, ly.w_up, M_up, dm, &eu));
         const dkv_epilogue ed = down_epi(L);
-        DKV_TRY(dkv_gemm(act, m->dtype, ly.w_down, m->dtype, round128(dm), N, m->d_ff, &ed, gwork, gemm_bytes, stream));
+        DKV_TRY(gemm(act, ly.w_down, round128(dm), m->d_ff, &ed));
     }
     if (!st->logits) return DKV_OK;        // prefill: the cache is written, no logits wanted
     if (!fused) DKV_TRY(dkv_norm(h, N, dm, llama ? 0 : 1, m->nf_w, m->nf_b, m->eps, x, m->dtype, stream));

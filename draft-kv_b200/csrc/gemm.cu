@@ -264,8 +264,14 @@ int launch_f32(const void* x, const void* w, int M, int N, int K, int S, const E
 
 }  // namespace
 
-extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K,
-                        const dkv_epilogue* epi, void* work, size_t work_bytes, void* stream) {
+namespace dkv {
+int choose_split_fill(int M, int N, int K);
+
+// dkv_gemm with `fill` set: a bf16 launch takes the K split that fills the
+// GPU for this N (choose_split_fill) instead of the one of (M, K) alone, for
+// rows that no other launch's rows are compared with (the prompt forward).
+int gemm_entry(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K, const dkv_epilogue* epi,
+               void* work, size_t work_bytes, void* stream, bool fill) {
     DKV_REQUIRE(x && w && epi && M > 0 && N >= 0 && K > 0, "dkv_gemm: bad arguments");
     DKV_REQUIRE(x_dtype == w_dtype, "dkv_gemm: x and w dtypes must match");
     DKV_REQUIRE(w_dtype == DKV_BF16 || w_dtype == DKV_F32, "dkv_gemm: dtype must be bf16 or f32");
@@ -280,7 +286,8 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     // algorithmic bytes: the weights once, the activations in and out
     const double elem = w_dtype == DKV_F32 ? 4.0 : 2.0;
     ProfScope ps(DKV_PROF_GEMM, (double)M_real * K * elem + (double)N * K * elem + (double)N * M_real * 4.0, st);
-    if (w_dtype == DKV_BF16) return gemm_tc(x, w, M, N, K, choose_split_tc(M, K), ea, st);
+    if (w_dtype == DKV_BF16)
+        return gemm_tc(x, w, M, N, K, fill ? choose_split_fill(M, N, K) : choose_split_tc(M, K), ea, st);
     const int mtiles = M / kTileM;
     const int S = choose_split(M, K);
     const int nblk = (N + kF32Tok - 1) / kF32Tok;
@@ -291,6 +298,12 @@ extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, 
     DKV_REQUIRE(tickets && (S == 1 || ws), "dkv_gemm: work buffer too small (%zu bytes, need %zu)", work_bytes,
                 dkv_gemm_work_bytes(M, N, K, w_dtype));
     return launch_f32(x, w, M, N, K, S, ea, ws, tickets, st);
+}
+}  // namespace dkv
+
+extern "C" int dkv_gemm(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K,
+                        const dkv_epilogue* epi, void* work, size_t work_bytes, void* stream) {
+    return dkv::gemm_entry(x, x_dtype, w, w_dtype, M, N, K, epi, work, work_bytes, stream, false);
 }
 
 // ---------------------------------------------------------------------------

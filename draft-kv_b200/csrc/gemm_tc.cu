@@ -479,6 +479,23 @@ int choose_split_tc(int M, int K) {
 // Token tile of a launch: N rounded up to 16 up to 64, 128 beyond.
 int tc_token_tile(int N) { return N <= 64 ? (N + 15) / 16 * 16 : 128; }
 
+// K split for a launch whose rows need not match any other launch's (the
+// prompt forward, whose rows feed only the cache): the least power of two
+// that fills the CTAs resident at once with row tiles x token blocks x S,
+// at most choose_split_tc(M, K).  A prompt chunk of 4 x 512 tokens runs
+// every Llama-3-8B projection unsplit (measured on B200, N = 2048: the QKV
+// and O projections at split 4 reach 297 and 292 TF/s).
+int choose_split_fill(int M, int N, int K) {
+    const int cap = choose_split_tc(M, K);
+    const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
+    const int NB = tc_token_tile(N);
+    const long long ctas = (long long)mtiles * ((N + NB - 1) / NB);
+    const int act = tc_active(1);
+    int S = 1;
+    while (S < cap && ctas * S < act) S *= 2;
+    return S;
+}
+
 size_t packed_weight_bytes_tc(int M, int K) { return (size_t)M * ((K + kTcKB - 1) / kTcKB) * kTcKB * 2; }
 
 int pack_weight_tc(const uint16_t* w, int M, int K, uint16_t* out, cudaStream_t st) {

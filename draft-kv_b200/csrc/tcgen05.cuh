@@ -138,6 +138,8 @@ DKV_DEV void named_sync(uint32_t id, uint32_t count) {
 int choose_split_tc(int M, int K);
 // Token tile of a launch (a multiple of 16).
 int tc_token_tile(int N);
+// K split of a launch that fills the GPU (rows compared with no other launch).
+int choose_split_fill(int M, int N, int K);
 // The cached 2-D tensor map of a bf16 token matrix X [N][K] with a box of
 // 64 k x NB rows (128-byte swizzle, zero fill past N and K).
 int token_map(const void* x, int N, int K, int NB, CUtensorMap* out);

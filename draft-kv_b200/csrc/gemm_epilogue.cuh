@@ -181,21 +181,26 @@ DKV_DEV void run_epilogue(const EpiArgs& e, float* T, int mtile, int n0, int nb,
 }
 
 // Input side of a fused RMSNorm: inv[j] for token rows j0 <= j < j1 of the
-// tile, summing the partials in part order (one thread a row; the caller
+// tile, summing the partials in part order (thread tid takes rows j0 + tid,
+// j0 + tid + nthr, ...: a 256-token tile has two rows a thread; the caller
 // syncs).
-DKV_DEV void epi_token_inv(const EpiArgs& e, int n0, int j0, int j1, float* inv, int tid = -1) {
-    const int j = j0 + (tid < 0 ? (int)threadIdx.x : tid);
-    if (j >= j1) return;
-    const float* p = e.norm_in_part + n0 + j;
-    float s = 0.f;
-    int t = 0;
-    for (; t + 4 <= e.norm_n_part; t += 4) {
-        const float a = p[(size_t)t * e.norm_ld], b = p[(size_t)(t + 1) * e.norm_ld];
-        const float c = p[(size_t)(t + 2) * e.norm_ld], d = p[(size_t)(t + 3) * e.norm_ld];
-        s = (((s + a) + b) + c) + d;
+DKV_DEV void epi_token_inv(const EpiArgs& e, int n0, int j0, int j1, float* inv, int tid = -1, int nthr = -1) {
+    if (tid < 0) {
+        tid = threadIdx.x;
+        nthr = blockDim.x;
     }
-    for (; t < e.norm_n_part; ++t) s += p[(size_t)t * e.norm_ld];
-    inv[j] = 1.0f / sqrtf(s / (float)e.norm_dm + e.norm_eps);
+    for (int j = j0 + tid; j < j1; j += nthr) {
+        const float* p = e.norm_in_part + n0 + j;
+        float s = 0.f;
+        int t = 0;
+        for (; t + 4 <= e.norm_n_part; t += 4) {
+            const float a = p[(size_t)t * e.norm_ld], b = p[(size_t)(t + 1) * e.norm_ld];
+            const float c = p[(size_t)(t + 2) * e.norm_ld], d = p[(size_t)(t + 3) * e.norm_ld];
+            s = (((s + a) + b) + c) + d;
+        }
+        for (; t < e.norm_n_part; ++t) s += p[(size_t)t * e.norm_ld];
+        inv[j] = 1.0f / sqrtf(s / (float)e.norm_dm + e.norm_eps);
+    }
 }
 
 // Output side: after run_epilogue left h_new^2 in T and the CTA synced, the

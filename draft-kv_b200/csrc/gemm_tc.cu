@@ -72,8 +72,12 @@ template <int NB>
 struct TcGeo {
     static_assert(NB % 16 == 0 && NB <= 256, "token tile");
     static constexpr int XBLK = NB * 128;                               // one k block of tokens
-    static constexpr int STAGE = kTcStageKB * (kTcBlockBytes + XBLK);   // multiple of 1024
-    static constexpr int BUDGET = DKV_TC_RING_BYTES;
+    // k blocks per stage: 2 (128 k), 1 for the 256-token tile (4 stages of
+    // 48 KB keep more copies in flight than 2 of 96 KB)
+    static constexpr int SKB = NB >= 256 ? 1 : kTcStageKB;
+    static constexpr int STAGE = SKB * (kTcBlockBytes + XBLK);   // multiple of 1024
+    // the 256-token tile runs one CTA per SM: 4 stages (192 KB)
+    static constexpr int BUDGET = NB >= 256 ? 4 * STAGE : DKV_TC_RING_BYTES;
     static constexpr int NST = STAGE * 5 <= BUDGET ? 5 : (STAGE * 4 <= BUDGET ? 4 : (STAGE * 3 <= BUDGET ? 3 : 2));
     static constexpr int TMEM_COLS = NB <= 32 ? 32 : (NB <= 64 ? 64 : (NB <= 128 ? 128 : 256));
     static constexpr size_t SMEM = (size_t)NST * STAGE + 1024;          // + alignment slack
@@ -108,7 +112,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int mtile = (int)(blockIdx.x / S) / nblks;
     const int nblk = (int)(blockIdx.x / S) % nblks, n0 = nblk * NB;
     const int kb0 = (int)((long long)s * g.KB / S), kb1 = (int)((long long)(s + 1) * g.KB / S);
-    const int nstages = (kb1 - kb0 + kTcStageKB - 1) / kTcStageKB;
+    const int nstages = (kb1 - kb0 + Geo::SKB - 1) / Geo::SKB;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -131,19 +135,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (warp == 0 && lane == 0) {
         // ---------------- producer
         const uint8_t* wsrc = g.w + ((size_t)mtile * g.KB + kb0) * kTcBlockBytes;
-        auto nkb_of = [&](int st) { return min(kTcStageKB, kb1 - kb0 - kTcStageKB * st); };
+        auto nkb_of = [&](int st) { return min(Geo::SKB, kb1 - kb0 - Geo::SKB * st); };
         auto issue_w = [&](int st) {
             const int slot = st % NST, nkb = nkb_of(st);
             uint8_t* dst = ring + (size_t)slot * Geo::STAGE;
             mbar_expect_tx(&full_bar[slot], (uint32_t)nkb * (kTcBlockBytes + Geo::XBLK));
-            bulk_g2s(dst, wsrc + (size_t)st * kTcStageKB * kTcBlockBytes, (uint32_t)nkb * kTcBlockBytes,
+            bulk_g2s(dst, wsrc + (size_t)st * Geo::SKB * kTcBlockBytes, (uint32_t)nkb * kTcBlockBytes,
                      &full_bar[slot]);
         };
         auto issue_x = [&](int st) {
             const int slot = st % NST, nkb = nkb_of(st);
-            uint8_t* dst = ring + (size_t)slot * Geo::STAGE + kTcStageKB * kTcBlockBytes;
+            uint8_t* dst = ring + (size_t)slot * Geo::STAGE + Geo::SKB * kTcBlockBytes;
             for (int j = 0; j < nkb; ++j)
-                tma_load_2d(dst + j * Geo::XBLK, &xmap, (kb0 + kTcStageKB * st + j) * kTcKB, n0, &full_bar[slot]);
+                tma_load_2d(dst + j * Geo::XBLK, &xmap, (kb0 + Geo::SKB * st + j) * kTcKB, n0, &full_bar[slot]);
         };
         const int pre = min(NST, nstages);
         for (int st = 0; st < pre; ++st) issue_w(st);
@@ -164,14 +168,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const uint32_t ring_s = smem_u32(ring);
         for (int st = 0; st < nstages; ++st) {
             const int slot = st % NST;
-            const int nkb = min(kTcStageKB, kb1 - kb0 - kTcStageKB * st);
+            const int nkb = min(Geo::SKB, kb1 - kb0 - Geo::SKB * st);
             if (!mbar_wait(&full_bar[slot], (uint32_t)((st / NST) & 1), g.err)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const uint32_t wbase = ring_s + slot * Geo::STAGE;
-            const uint32_t xbase = wbase + kTcStageKB * kTcBlockBytes;
+            const uint32_t xbase = wbase + Geo::SKB * kTcBlockBytes;
             for (int j = 0; j < nkb; ++j) {
 #pragma unroll
                 for (int k16 = 0; k16 < kTcKB / 16; ++k16)
@@ -476,13 +480,16 @@ int choose_split_tc(int M, int K) {
     return best;
 }
 
-// Token tile of a launch: N rounded up to 16 up to 64, 128 beyond.
-int tc_token_tile(int N) { return N <= 64 ? (N + 15) / 16 * 16 : 128; }
+// Token tile of a launch: N rounded up to 16 up to 64, 128 up to 512, 256
+// beyond (a prompt chunk: an MMA of N = 256 reads 12 KB of operands per
+// 128 x 256 x 16 product, 94 bytes a clock at the tensor rate, where N = 128
+// needs the full 128 bytes a clock of shared memory).
+int tc_token_tile(int N) { return N <= 64 ? (N + 15) / 16 * 16 : (N <= 512 ? 128 : 256); }
 
 // K split for a launch whose rows need not match any other launch's (the
 // prompt forward, whose rows feed only the cache): the least power of two
-// that fills the CTAs resident at once with row tiles x token blocks x S,
-// at most choose_split_tc(M, K).  A prompt chunk of 4 x 512 tokens runs
+// that gives row tiles x token blocks x S two waves of the CTAs resident at
+// once, at most choose_split_tc(M, K).  A prompt chunk of 4 x 512 tokens runs
 // every Llama-3-8B projection unsplit (measured on B200, N = 2048: the QKV
 // and O projections at split 4 reach 297 and 292 TF/s).
 int choose_split_fill(int M, int N, int K) {
@@ -490,9 +497,11 @@ int choose_split_fill(int M, int N, int K) {
     const int mtiles = M / kTileM > 0 ? M / kTileM : 1;
     const int NB = tc_token_tile(N);
     const long long ctas = (long long)mtiles * ((N + NB - 1) / NB);
-    const int act = tc_active(1);
+    // CTAs resident at once (the 256-token tile runs one per SM); at least
+    // two waves, so that no SM idles through a long last wave
+    const int act = NB >= 256 ? tc_active(1) / 2 : tc_active(1);
     int S = 1;
-    while (S < cap && ctas * S < act) S *= 2;
+    while (S < cap && ctas * S < 2 * act) S *= 2;
     return S;
 }
 
@@ -532,7 +541,8 @@ int gemm_tc(const void* x, const void* w, int M, int N, int K, int S, const EpiA
         case 32: e = tc_launch<32>(map, g, mtiles, nblk, st); break;
         case 48: e = tc_launch<48>(map, g, mtiles, nblk, st); break;
         case 64: e = tc_launch<64>(map, g, mtiles, nblk, st); break;
-        default: e = tc_launch<128>(map, g, mtiles, nblk, st); break;
+        case 128: e = tc_launch<128>(map, g, mtiles, nblk, st); break;
+        default: e = tc_launch<256>(map, g, mtiles, nblk, st); break;
     }
     DKV_CUDA(e);
     DKV_LAUNCHED();

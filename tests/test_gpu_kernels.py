@@ -249,21 +249,22 @@ def test_bf16_gemm_matches_torch_and_is_batch_invariant(M, K):
     g = torch.Generator(device="cuda").manual_seed(M + K)
     W = (torch.randn((M, K), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
     Wt = L.pack_weight(W)
-    X = torch.randn((100, K), generator=g, device="cuda").to(torch.bfloat16)
+    X = torch.randn((1100, K), generator=g, device="cuda").to(torch.bfloat16)
     ref = X.float() @ W.float().t()
     outs = {}
-    for N in (1, 5, 37, 64, 100):
+    for N in (1, 5, 37, 64, 100, 300, 1100):    # token tiles of 16 .. 64, 128 and 256
         out = torch.zeros((N, M), dtype=torch.float32, device="cuda")
         _gemm(X[:N].contiguous(), Wt, M, N, K, L.EPI_STORE, L.BF16, out=out, ld=M)
         torch.testing.assert_close(out, ref[:N], rtol=1e-4, atol=1e-4)
         outs[N] = out
-    for N in (5, 37, 64, 100):     # token 0's column is bit-identical whatever N
+    for N in (5, 37, 64, 100, 300, 1100):     # token 0's column is bit-identical whatever N
         assert torch.equal(outs[N][0], outs[1][0])
     assert torch.equal(outs[100][:64], outs[64])
+    assert torch.equal(outs[1100][:300], outs[300])
 
 
 @pytest.mark.parametrize("M,K", [(4096, 4096), (1024, 512)])
-@pytest.mark.parametrize("N", [4, 36])
+@pytest.mark.parametrize("N", [4, 36, 600])
 def test_fused_rmsnorm_epilogues(M, K, N):
     """The two halves of the RMSNorm fused into the bf16 GEMM (llama.py:93-94).
     Output side (RESADD): h_new = h + X W^T + b, xn = bf16(h_new * w) and the

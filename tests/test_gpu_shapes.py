@@ -151,6 +151,41 @@ def test_llama3_8b_slice_verify_rows_equal_decode_rows_long_context(l8):
         assert torch.equal(blk[:, i], rows[i]), i
 
 
+def test_llama3_8b_slice_prompt_forward_matches_logit_path(l8):
+    """The prompt forward of long prompts -- chunks of 512 tokens x batch 2
+    (1024-token launches: 256-token GEMM tiles, the K split that fills the
+    GPU, the tcgen05 prefill attention, no logits) -- writes the cache the
+    logits path writes 64 tokens at a time (token tiles of 64, the splits of
+    (M, K), the oracle-pinned path of test_llama3_8b_slice_logits_bf16): K and
+    V of every layer within 2e-2 of each other's scale, and the next token's
+    logits within 2e-2."""
+    from draftkv import DraftKVEngine, FullKVCache
+    m, _ = l8
+    B, n0 = 2, 1100
+    prompts = [W.tokens(n0, m.vocab_size, seed=20 + b) for b in range(B)]
+    st = DraftKVEngine(m, seed=0)._start(prompts, 8, 0.0)       # 1099 prompt rows: 512-token chunks
+    refs = []
+    for b in range(B):
+        ref = FullKVCache(m.n_layers)
+        for c0 in range(0, n0 - 1, 64):
+            m.forward(np.array(prompts[b][c0:min(n0 - 1, c0 + 64)]), ref, c0)
+        for L in range(m.n_layers):
+            k1, v1, _ = st.full.read(L, b)
+            k2, v2, _ = ref.read(L, b=0)
+            assert k1.shape == k2.shape == (n0 - 1, m.n_kv_heads, m.d_head)
+            assert rel_err(k1, k2) < 2e-2 and rel_err(v1, v2) < 2e-2, (b, L)
+        refs.append(ref)
+    # the last prompt token over each cache
+    cap = st.full.capacity_tokens
+    work = m.work(B, 1, cap, 0)
+    rows = torch.empty((B, m.vocab_size), dtype=torch.float32, device="cuda")
+    m.forward_raw(st.full, None, st.vtok.data_ptr(), st.VS, st.base_pos, B, 1, rows, work, 1, cap)
+    torch.cuda.synchronize()
+    for b in range(B):
+        want = m.forward(np.array([prompts[b][-1]]), refs[b], n0 - 1).cpu().numpy()
+        assert rel_err(rows[b].cpu().numpy(), want[0]) < 2e-2, b
+
+
 # ---------------------------------------------------------------- head GEMM
 def test_head_gemm_many_waves_match_torch():
     """The 128256 x 4096 head: 1002 row tiles, several waves of CTAs.

@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--settle S] [--config c4|c3|c1|small]
                     [--impl draftkv|reference]
-    python bench.py --kernel draft-attn|verify-attn|gemm|gemm-layer [--batch B --ctx C --bits b
+    python bench.py --kernel draft-attn|verify-attn|prefill-attn|gemm|gemm-layer [--batch B --ctx C --bits b
                     --keep f --T t --M m --K k --N n --iters i]     (one kernel alone)
 
 A step is R (--rounds-per-step, default 10) draft / verify rounds over every
@@ -905,6 +905,9 @@ def run_kernel(args) -> None:
       draft-attn   drafter attention (configuration 2 shape by default:
                    batch 32, ctx 32768, 8 kv x 128, group 4, int4 keep 0.25)
       verify-attn  full-cache attention for T query tokens per sequence
+      prefill-attn the same for a prompt chunk (T = 512 tokens at the end of
+                   the context, pages in the block pool's allocation order,
+                   8192-key splits): the tcgen05 prefill kernel, in TF/s
       gemm         weight-streaming GEMM, M x K weights, N tokens
       gemm-layer   the four projections of a decoder layer (Llama-3-8B shape:
                    QKV, O, gate/up, down) back to back as the forward launches
@@ -948,7 +951,7 @@ def run_kernel(args) -> None:
         full = FullKVCache(1, n_kv, d, "bf16", capacity=ctx + 64, batch=B)
         for b in range(B):
             full.ensure(b, ctx + 16)
-        if not args.no_shuffle:
+        if not (args.no_shuffle or args.kernel == "prefill-attn"):
             # configuration 2: the page table shuffled from a seed (pages of a
             # sequence scattered over the pool)
             used = sorted({blk for b in range(B) for blk in full.block_tables[b][0]})
@@ -990,10 +993,12 @@ def run_kernel(args) -> None:
                                       out.data_ptr(), _lib.BF16, work.data_ptr(), work.numel(), _lib.stream_ptr()))
         line["config"] = {"batch": B, "ctx": ctx, "kept": kept, "bits": args.bits, "keep": args.keep,
                           "n_kv": n_kv, "d_head": d, "group": G}
-    elif args.kernel == "verify-attn":
+    elif args.kernel in ("verify-attn", "prefill-attn"):
         full = full_cache()
-        T = args.T
-        work = torch.zeros(int(_lib.load().dkv_attn_work_bytes(full.dims(), G, T, ctx + 64, args.split, 0)),
+        prefill = args.kernel == "prefill-attn"
+        T = args.T or (512 if prefill else 9)
+        split = args.split or (8192 if prefill else 512)
+        work = torch.zeros(int(_lib.load().dkv_attn_work_bytes(full.dims(), G, T, ctx + 64, split, 0)),
                            dtype=torch.uint8, device="cuda")
         qv = torch.randn((B * T, n_kv * G, d), device="cuda")
         p0 = torch.full((B,), ctx - T, dtype=torch.int32, device="cuda")
@@ -1002,10 +1007,10 @@ def run_kernel(args) -> None:
         # causal: query t (position ctx - T + t) sees ctx - T + t + 1 keys; 4 flops a (key, dim) pair
         line["flops"] = B * n_kv * G * sum(ctx - T + t + 1 for t in range(T)) * d * 4
         us = timeit(lambda: _lib.call("dkv_attn_full", full.struct(), full.dims(), 0, G, T, qv.data_ptr(),
-                                      p0.data_ptr(), outv.data_ptr(), _lib.BF16, args.split, work.data_ptr(), work.numel(),
+                                      p0.data_ptr(), outv.data_ptr(), _lib.BF16, split, work.data_ptr(), work.numel(),
                                       _lib.stream_ptr()))
-        line["config"] = {"batch": B, "ctx": ctx, "T": T, "n_kv": n_kv, "d_head": d, "group": G, "split": args.split,
-                          "pages": "sequential" if args.no_shuffle else "shuffled (seed 7)"}
+        line["config"] = {"batch": B, "ctx": ctx, "T": T, "n_kv": n_kv, "d_head": d, "group": G, "split": split,
+                          "pages": "allocation order" if (args.no_shuffle or prefill) else "shuffled (seed 7)"}
     elif args.kernel == "gemm-layer":
         N, NL = args.N, 8
         shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
@@ -1106,16 +1111,16 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-calibrate", action="store_true",
                     help="keep the cost model's default fixed costs instead of measuring them on the device")
-    ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "gemm", "gemm-layer"], default=None,
+    ap.add_argument("--kernel", choices=["draft-attn", "verify-attn", "prefill-attn", "gemm", "gemm-layer"], default=None,
                     help="time one kernel alone on a synthetic case instead of the decode step")
     ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--keep", type=float, default=0.25)
-    ap.add_argument("--T", type=int, default=9)
+    ap.add_argument("--T", type=int, default=None, help="query tokens (verify-attn 9, prefill-attn 512)")
     ap.add_argument("--M", type=int, default=28672)
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--N", type=int, default=4)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--split", type=int, default=512, help="keys per split (verify-attn)")
+    ap.add_argument("--split", type=int, default=None, help="keys per split (verify-attn 512, prefill-attn 8192)")
     ap.add_argument("--no-shuffle", action="store_true", help="kernel mode: keep the page table in allocation order")
     args = ap.parse_args()
     if args.kernel:

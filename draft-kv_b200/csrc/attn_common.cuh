@@ -94,14 +94,43 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
     if (!is_last) return false;
     __threadfence();
     const float* parts = a.part + (bhr * a.n_splits) * RB * PS;
+    // per (row, split) weight exp(m_q - M), -1 for a split with no live key;
+    // with up to kMergeW splits the weights sit in shared memory and an
+    // element's partials are all loaded before the sum (the same products in
+    // the same split order as the loop below, so the same bits)
+    constexpr int kMergeW = 16;
+    __shared__ float wq[RB * kMergeW];
+    const int ns = a.n_splits;
+    const bool staged = ns <= kMergeW;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
-        float M = -INFINITY;
-        for (int q = 0; q < a.n_splits; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * RB + r) * PS));
-        float L = 0.f;
-        for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
-            if (mq == -INFINITY) continue;
-            L += __ldcg(parts + ((size_t)q * RB + r) * PS + 1) * expf(mq - M);
+        float M = -INFINITY, L = 0.f;
+        if (staged) {
+            float mq[kMergeW], lq[kMergeW];
+#pragma unroll
+            for (int q = 0; q < kMergeW; ++q) {
+                mq[q] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS) : -INFINITY;
+                lq[q] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS + 1) : 0.f;
+            }
+#pragma unroll
+            for (int q = 0; q < kMergeW; ++q) M = fmaxf(M, mq[q]);
+#pragma unroll
+            for (int q = 0; q < kMergeW; ++q) {
+                if (q >= ns) break;
+                if (mq[q] == -INFINITY) {
+                    wq[r * kMergeW + q] = -1.f;
+                    continue;
+                }
+                const float w = expf(mq[q] - M);
+                wq[r * kMergeW + q] = w;
+                L += lq[q] * w;
+            }
+        } else {
+            for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * RB + r) * PS));
+            for (int q = 0; q < ns; ++q) {
+                const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
+                if (mq == -INFINITY) continue;
+                L += __ldcg(parts + ((size_t)q * RB + r) * PS + 1) * expf(mq - M);
+            }
         }
         ms[r] = M;
         ls[r] = L;
@@ -109,12 +138,24 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
     __syncthreads();
     for (int i = threadIdx.x; i < R * d; i += blockDim.x) {
         const int r = i / d, e = i % d;
-        const float M = ms[r];
         float acc = 0.f;
-        for (int q = 0; q < a.n_splits; ++q) {
-            const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
-            if (mq == -INFINITY) continue;
-            acc += __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) * expf(mq - M);
+        if (staged) {
+            float v[kMergeW];
+#pragma unroll
+            for (int q = 0; q < kMergeW; ++q)
+                v[q] = (q < ns && wq[r * kMergeW + q] >= 0.f) ? __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) : 0.f;
+#pragma unroll
+            for (int q = 0; q < kMergeW; ++q) {
+                const float w = q < ns ? wq[r * kMergeW + q] : -1.f;
+                if (w >= 0.f) acc += v[q] * w;
+            }
+        } else {
+            const float M = ms[r];
+            for (int q = 0; q < ns; ++q) {
+                const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
+                if (mq == -INFINITY) continue;
+                acc += __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) * expf(mq - M);
+            }
         }
         const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
         const int t = (r0 + r) / G, g = (r0 + r) % G;

@@ -95,13 +95,13 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
     __threadfence();
     const float* parts = a.part + (bhr * a.n_splits) * RB * PS;
     // per (row, split) weight exp(m_q - M), -1 for a split with no live key;
-    // with up to kMergeW splits the weights sit in shared memory and an
-    // element's partials are all loaded before the sum (the same products in
-    // the same split order as the loop below, so the same bits)
+    // with up to kMergeW splits the weights sit in shared memory and the
+    // partials of several elements are loaded at once (the same products in
+    // the same split order as the one-element loop, so the same bits)
     constexpr int kMergeW = 16;
     __shared__ float wq[RB * kMergeW];
     const int ns = a.n_splits;
-    const bool staged = ns <= kMergeW;
+    const bool staged = ns <= kMergeW && d % 2 == 0;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float M = -INFINITY, L = 0.f;
         if (staged) {
@@ -136,30 +136,64 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
         ls[r] = L;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < R * d; i += blockDim.x) {
-        const int r = i / d, e = i % d;
-        float acc = 0.f;
-        if (staged) {
-            float v[kMergeW];
+    if (staged) {
+        // element pairs (e, e + 1), kMergeP of them a thread in flight: a
+        // split's kMergeP loads are issued together, each element summed over
+        // the splits in split order
+        constexpr int kMergeP = 8;
+        const int npairs = R * d / 2;
+        for (int p0 = threadIdx.x; p0 < npairs; p0 += kMergeP * blockDim.x) {
+            float2 acc[kMergeP];
+            int rr[kMergeP], ee[kMergeP];
 #pragma unroll
-            for (int q = 0; q < kMergeW; ++q)
-                v[q] = (q < ns && wq[r * kMergeW + q] >= 0.f) ? __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) : 0.f;
-#pragma unroll
-            for (int q = 0; q < kMergeW; ++q) {
-                const float w = q < ns ? wq[r * kMergeW + q] : -1.f;
-                if (w >= 0.f) acc += v[q] * w;
+            for (int u = 0; u < kMergeP; ++u) {
+                const int pi = p0 + u * blockDim.x;
+                rr[u] = pi < npairs ? 2 * pi / d : -1;
+                ee[u] = pi < npairs ? 2 * pi % d : 0;
+                acc[u] = make_float2(0.f, 0.f);
             }
-        } else {
+            for (int q = 0; q < ns; ++q) {
+                float2 v[kMergeP];
+                float w[kMergeP];
+#pragma unroll
+                for (int u = 0; u < kMergeP; ++u) {
+                    w[u] = rr[u] >= 0 ? wq[rr[u] * kMergeW + q] : -1.f;
+                    v[u] = w[u] >= 0.f ? __ldcg(reinterpret_cast<const float2*>(
+                                             parts + ((size_t)q * RB + rr[u]) * PS + 2 + ee[u]))
+                                       : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kMergeP; ++u)
+                    if (w[u] >= 0.f) {
+                        acc[u].x += v[u].x * w[u];
+                        acc[u].y += v[u].y * w[u];
+                    }
+            }
+#pragma unroll
+            for (int u = 0; u < kMergeP; ++u) {
+                if (rr[u] < 0) continue;
+                const int r = rr[u], e = ee[u];
+                const float L = ls[r];
+                const int t = (r0 + r) / G, g = (r0 + r) % G;
+                const size_t o = (((size_t)b * T + t) * HQ + h * G + g) * d + e;
+                store_from_f32(a.out, a.out_dtype, o, L > 0.f ? acc[u].x / L : 0.f);
+                store_from_f32(a.out, a.out_dtype, o + 1, L > 0.f ? acc[u].y / L : 0.f);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < R * d; i += blockDim.x) {
+            const int r = i / d, e = i % d;
             const float M = ms[r];
+            float acc = 0.f;
             for (int q = 0; q < ns; ++q) {
                 const float mq = __ldcg(parts + ((size_t)q * RB + r) * PS);
                 if (mq == -INFINITY) continue;
                 acc += __ldcg(parts + ((size_t)q * RB + r) * PS + 2 + e) * expf(mq - M);
             }
+            const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
+            const int t = (r0 + r) / G, g = (r0 + r) % G;
+            store_from_f32(a.out, a.out_dtype, (((size_t)b * T + t) * HQ + h * G + g) * d + e, o);
         }
-        const float o = ls[r] > 0.f ? acc / ls[r] : 0.f;
-        const int t = (r0 + r) / G, g = (r0 + r) % G;
-        store_from_f32(a.out, a.out_dtype, (((size_t)b * T + t) * HQ + h * G + g) * d + e, o);
     }
     __syncthreads();
     return true;

@@ -108,6 +108,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     const int HQ = a.n_kv * G;
     const size_t bhr = ((size_t)b * a.n_kv + h) * a.n_rb + rb;
 
+    pdl_trigger();
+    pdl_wait();      // the queries and the chunk's cache rows come from earlier kernels
+    const int qbase = a.qpos0[b];
+    const int n_keys = qbase + T;
+    const int k0 = s * a.split;                         // a multiple of 128
+    const int tmax = (r0 + R - 1) / G;                  // this CTA's last token
+    const int kend = min(min(n_keys, k0 + a.split), qbase + tmax + 1);
+    const int ntiles = kend > k0 ? (kend - k0 + kPfKeys - 1) / kPfKeys : 0;
+    if (ntiles == 0) {
+        // no key of this split is visible to these rows (early prompt
+        // chunks leave most splits of a long pool empty): empty partials and
+        // the merge ticket only
+        for (int r = threadIdx.x; r < R; r += blockDim.x) {
+            float* mypart = a.part + ((bhr * a.n_splits + s) * kPfRows + r) * PS;
+            mypart[0] = -INFINITY;
+            mypart[1] = 0.f;
+        }
+        split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, reinterpret_cast<float*>(sm),
+                             (int)(2 * kPfNst * Geo::KVB / 4));
+        return;
+    }
+
     if (threadIdx.x == 0) {
         for (int i = 0; i < kPfNst; ++i) {
             mbar_init(&k_full[i], 1);
@@ -128,17 +150,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    pdl_trigger();
-    pdl_wait();      // the queries and the chunk's cache rows come from earlier kernels
-
-    const int qbase = a.qpos0[b];
-    const int n_keys = qbase + T;
-    const int k0 = s * a.split;                         // a multiple of 128
-    const int tmax = (r0 + R - 1) / G;                  // this CTA's last token
-    const int kend = min(min(n_keys, k0 + a.split), qbase + tmax + 1);
-    const int ntiles = kend > k0 ? (kend - k0 + kPfKeys - 1) / kPfKeys : 0;
     const int32_t* ptab = a.src.page_table + ((size_t)b * a.n_layers + a.layer) * a.src.max_pages;
-    const int npg = kend > k0 ? (kend - k0 + 15) / 16 : 0;
+    const int npg = (kend - k0 + 15) / 16;
     const bool staged = npg <= kPfSplitPages;
 
     bool ok = true;
@@ -424,7 +437,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     }
     // after a failure (error word set) every row of this split is empty, and
     // the merge still runs so that the tickets stay consistent
-    split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls);
+    // the drained rings hold the merge's per-(row, split) weights
+    split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, all_ok ? reinterpret_cast<float*>(sm) : nullptr,
+                         (int)(2 * kPfNst * Geo::KVB / 4));
 }
 
 // Host: the prefill launch of dkv_attn_full (rows > 64, bf16 pool in device

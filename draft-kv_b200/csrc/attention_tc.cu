@@ -580,7 +580,9 @@ __global__ void __launch_bounds__(MAXT, 2) attn_kq_kernel(const __grid_constant_
             mypart[(size_t)r * PS + 2 + e] = acc;
         }
     }
-    split_merge(a, bhr, b, h, R, rbase, ms, ls);
+    // the drained ring holds the merge's per-(row, split) weights
+    split_merge(a, bhr, b, h, R, rbase, ms, ls, ok_all ? reinterpret_cast<float*>(tsm) : nullptr,
+                (int)(kKqNST * 2 * kTcKT * D * 2 / 4));
 }
 
 template <int D>

@@ -77,9 +77,12 @@ DKV_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z,
 // rows and returns true with the merged max / sum in ms / ls (R rows).
 // The merge order is fixed, so a row's result is the same whatever the number
 // of rows or splits that share the launch.  RB: the row stride of a split's
-// partial block (the launch's rows per CTA).
+// partial block (the launch's rows per CTA).  wbuf / wcap: shared memory
+// the caller no longer needs (its drained ring), floats; without it the
+// weights of up to 16 splits go to a static array.
 template <int RB = kAttnRB>
-DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int r0, float* ms, float* ls) {
+DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int r0, float* ms, float* ls,
+                         float* wbuf = nullptr, int wcap = 0) {
     const int d = a.d, G = a.group, T = a.T, PS = d + 2, HQ = a.n_kv * G;
     __threadfence();
     __syncthreads();
@@ -99,30 +102,44 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
     // partials of several elements are loaded at once (the same products in
     // the same split order as the one-element loop, so the same bits)
     constexpr int kMergeW = 16;
-    __shared__ float wq[RB * kMergeW];
+    __shared__ float wq_s[RB * kMergeW];
     const int ns = a.n_splits;
-    const bool staged = ns <= kMergeW && d % 2 == 0;
+    const bool big = wbuf && ns > kMergeW && (long long)ns * RB <= wcap;
+    float* wq = big ? wbuf : wq_s;
+    const int wst = big ? ns : kMergeW;       // row stride of wq
+    const bool staged = (big || ns <= kMergeW) && d % 2 == 0;
     for (int r = threadIdx.x; r < R; r += blockDim.x) {
         float M = -INFINITY, L = 0.f;
         if (staged) {
-            float mq[kMergeW], lq[kMergeW];
+            // splits in groups of kMergeW, each group's loads issued together:
+            // the max first, then the weights and the sum in split order
+            for (int q0 = 0; q0 < ns; q0 += kMergeW) {
+                float mq[kMergeW];
 #pragma unroll
-            for (int q = 0; q < kMergeW; ++q) {
-                mq[q] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS) : -INFINITY;
-                lq[q] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS + 1) : 0.f;
+                for (int k = 0; k < kMergeW; ++k)
+                    mq[k] = q0 + k < ns ? __ldcg(parts + ((size_t)(q0 + k) * RB + r) * PS) : -INFINITY;
+#pragma unroll
+                for (int k = 0; k < kMergeW; ++k) M = fmaxf(M, mq[k]);
             }
+            for (int q0 = 0; q0 < ns; q0 += kMergeW) {
+                float mq[kMergeW], lq[kMergeW];
 #pragma unroll
-            for (int q = 0; q < kMergeW; ++q) M = fmaxf(M, mq[q]);
-#pragma unroll
-            for (int q = 0; q < kMergeW; ++q) {
-                if (q >= ns) break;
-                if (mq[q] == -INFINITY) {
-                    wq[r * kMergeW + q] = -1.f;
-                    continue;
+                for (int k = 0; k < kMergeW; ++k) {
+                    const int q = q0 + k;
+                    mq[k] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS) : -INFINITY;
+                    lq[k] = q < ns ? __ldcg(parts + ((size_t)q * RB + r) * PS + 1) : 0.f;
                 }
-                const float w = expf(mq[q] - M);
-                wq[r * kMergeW + q] = w;
-                L += lq[q] * w;
+#pragma unroll
+                for (int k = 0; k < kMergeW; ++k) {
+                    if (q0 + k >= ns) break;
+                    if (mq[k] == -INFINITY) {
+                        wq[r * wst + q0 + k] = -1.f;
+                        continue;
+                    }
+                    const float w = expf(mq[k] - M);
+                    wq[r * wst + q0 + k] = w;
+                    L += lq[k] * w;
+                }
             }
         } else {
             for (int q = 0; q < ns; ++q) M = fmaxf(M, __ldcg(parts + ((size_t)q * RB + r) * PS));
@@ -164,7 +181,7 @@ DKV_DEV bool split_merge(const AttnArgs& a, size_t bhr, int b, int h, int R, int
 #pragma unroll
                     for (int u = 0; u < kMergeP; ++u) {
                         const int q = q0 + k;
-                        w[k][u] = (q < ns && rr[u] >= 0) ? wq[rr[u] * kMergeW + (q < kMergeW ? q : 0)] : -1.f;
+                        w[k][u] = (q < ns && rr[u] >= 0) ? wq[rr[u] * wst + (q < ns ? q : 0)] : -1.f;
                         v[k][u] = w[k][u] >= 0.f ? __ldcg(reinterpret_cast<const float2*>(
                                                        parts + ((size_t)q * RB + rr[u]) * PS + 2 + ee[u]))
                                                  : make_float2(0.f, 0.f);

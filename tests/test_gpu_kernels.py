@@ -491,7 +491,9 @@ def test_full_attention_matches_torch_and_decode(dtype, G, d):
     L = lib()
     n_kv, n = 2, 700
     code = L.F32 if dtype == "f32" else L.BF16
-    cache = PagedKVCache(1, n_kv, d, 16, 64, dtype, batch=1)
+    # 160 pages: 20 splits of 128 keys, past the merge's static 16 (the
+    # tensor-core kernel stages the split weights in its drained ring)
+    cache = PagedKVCache(1, n_kv, d, 16, 160, dtype, batch=1)
     rng = np.random.default_rng(G)
     k = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
     v = round_bf16(rng.standard_normal((n, n_kv, d)).astype(np.float32))
@@ -525,7 +527,7 @@ def test_full_attention_matches_torch_and_decode(dtype, G, d):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("G", [1, 4])
-@pytest.mark.parametrize("n,T,split", [(700, 700, 3648), (1000, 37, 256), (4100, 300, 1024)])
+@pytest.mark.parametrize("n,T,split", [(700, 700, 3648), (1000, 37, 256), (4100, 300, 1024), (4100, 300, 128)])
 def test_prefill_attention_matches_torch(d, G, n, T, split):
     """The tcgen05 prefill kernel (more than 64 query rows, bf16 pool in
     device memory): causal GQA attention of T new tokens at positions
@@ -535,8 +537,10 @@ def test_prefill_attention_matches_torch(d, G, n, T, split):
     splits and lazy rescale) moves single outputs by up to 1.24e-2 and the
     mean by 2.5e-4 to 5.8e-4.  Cases: a whole 700-token prompt (ragged last
     row block, one split), 37 tokens over 1000 keys in 256-key splits (rows
-    whose split starts past their position), 300 tokens over 4100 keys;
-    every context ends inside a page whose unused rows hold NaN."""
+    whose split starts past their position), 300 tokens over 4100 keys in
+    1024- and 128-key splits (35 splits: the merge stages its weights in the
+    drained ring; splits past the rows' positions exit early); every context
+    ends inside a page whose unused rows hold NaN."""
     from draftkv import PagedKVCache
     L = lib()
     n_kv = 2

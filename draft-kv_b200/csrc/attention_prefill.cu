@@ -70,6 +70,30 @@ DKV_DEV float pf_ex2(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
     return y;
 }
+DKV_DEV float pf_max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+// two fp32 lanes in one 64-bit register, and the sm_100 packed add / subtract
+DKV_DEV uint64_t pf_pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+DKV_DEV void pf_unpack2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;\n" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+DKV_DEV uint64_t pf_add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+DKV_DEV uint64_t pf_sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
 DKV_DEV void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -335,31 +359,45 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                     for (int e = 0; e < 32; ++e)
                         if (c * 32 + e > lc) sr[c][e] = __float_as_uint(-INFINITY);
             }
-            float mx[4];
+            // row max: 8 chains of three-input max
+            float mx[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                mx[c] = __uint_as_float(sr[c][0]);
+            for (int k = 0; k < 8; ++k) mx[k] = __uint_as_float(sr[k >> 1][(k & 1) * 16]);
 #pragma unroll
-                for (int e = 1; e < 32; ++e) mx[c] = fmaxf(mx[c], __uint_as_float(sr[c][e]));
-            }
-            const float mn = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+            for (int k = 0; k < 8; ++k)
+#pragma unroll
+                for (int e = 1; e < 16; e += 2)
+                    mx[k] = pf_max3(mx[k], __uint_as_float(sr[k >> 1][(k & 1) * 16 + e]),
+                                    e + 1 < 16 ? __uint_as_float(sr[k >> 1][(k & 1) * 16 + e + 1]) : mx[k]);
+            const float mn = fmaxf(m, pf_max3(pf_max3(mx[0], mx[1], mx[2]), pf_max3(mx[3], mx[4], mx[5]),
+                                              fmaxf(mx[6], mx[7])));
             float alpha = 1.f;
             if (m == -INFINITY || mn > m + kPfRescale) {
                 alpha = m == -INFINITY ? 0.f : pf_ex2(m - mn);
                 m = mn;
             }
             const float msub = m == -INFINITY ? 0.f : m;
-            float sum[4] = {0.f, 0.f, 0.f, 0.f};
+            // exp2(s - m) two at a time: packed subtract and sum (f32x2)
+            const uint64_t mm = pf_pack2(msub, msub);
+            uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
             uint32_t pk[2][32];
 #pragma unroll
             for (int c = 0; c < 4; ++c)
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = pf_ex2(__uint_as_float(sr[c][e]) - msub);
-                    const float p1 = pf_ex2(__uint_as_float(sr[c][e + 1]) - msub);
-                    sum[c] += p0 + p1;
+                    float d0, d1;
+                    pf_unpack2(pf_sub2(pf_pack2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), mm), d0, d1);
+                    const float p0 = pf_ex2(d0), p1 = pf_ex2(d1);
+                    sum2[c] = pf_add2(sum2[c], pf_pack2(p0, p1));
                     pk[c >> 1][(c & 1) * 16 + e / 2] = pf_pack(p0, p1);
                 }
+            float sum[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float a0, a1;
+                pf_unpack2(sum2[c], a0, a1);
+                sum[c] = a0 + a1;
+            }
             l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
             if (j >= 1) {
                 // P_{j-1} V_{j-1} has updated O (the waits stay in phase order)

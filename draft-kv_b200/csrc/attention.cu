@@ -257,10 +257,10 @@ constexpr size_t kAttnTickets = 16384;
 static size_t attn_scratch(int batch, int n_kv, int n_splits, int R, int d, int cap, int group, bool comp) {
     // row blocks: up to 64 rows the tensor-core kernel takes 16 rows a CTA
     // (each block keeps a 64-row partial stride); beyond that the prefill
-    // kernel takes 128 rows a CTA (counted as two 64-row blocks, which also
+    // kernel takes 256 rows a CTA (counted as four 64-row blocks, which also
     // covers the 64-row kernels)
     const int n_rb = comp ? (R + kGenRB - 1) / kGenRB
-                          : (R <= kGenRB ? (R + 15) / 16 : 2 * ((R + 2 * kGenRB - 1) / (2 * kGenRB)));
+                          : (R <= kGenRB ? (R + 15) / 16 : 4 * ((R + 4 * kGenRB - 1) / (4 * kGenRB)));
     size_t b = kAttnTickets * sizeof(unsigned);
     b += align_up((size_t)batch * n_kv * n_rb * n_splits * kGenRB * (d + 2) * sizeof(float), 256);
     if (comp) b += align_up((size_t)batch * n_kv * group * cap * sizeof(float), 256);

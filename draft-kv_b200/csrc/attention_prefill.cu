@@ -3,31 +3,33 @@
 // memory).  Replaces the attention of the prompt forward (draftkv/engine.py:
 // 133-134 running draftkv/llama.py:202-219 over every prompt position).
 //
-// One CTA per (sequence, KV head, key split, block of 128 query rows), rows =
-// token x GQA head as in the other attention kernels; 6 warps:
-//   warp 4 -- producer: per 128-key tile, one copy of 128 keys x 64 dims
+// One CTA per (sequence, KV head, key split, block of 256 query rows: query
+// tiles A and B of 128), rows = token x GQA head as in the other attention
+// kernels; 10 warps, one CTA per SM:
+//   warp 8 -- producer: per 128-key tile, one copy of 128 keys x 64 dims
 //     when the tile's 8 pages are consecutive in the pool (ascending, or
 //     descending for a tile no row masks), else 8 lanes issue one page each
 //     (16 keys x 64 dims, 2 KB; one copy engine serves the SM at ~90 cycles a
-//     2 KB box, so fewer, larger boxes are faster); 128-byte swizzle, 3-deep
+//     2 KB box, so fewer, larger boxes are faster); 128-byte swizzle, 2-deep
 //     K and V rings; pages wholly past the CTA's last key are read past the
-//     pool view (zeros).  K_j is copied once S_{j-3} has read its slot, V_{j-1} once
-//     P_{j-4} V_{j-4} has;
-//   warp 5 -- TMEM allocation; lane 0 issues the MMAs: S_j = Q K_j^T into
-//     one of two 128-column TMEM buffers (M 128 rows, N 128 keys, K = d; Q in
-//     TMEM), then O += P_{j-1} V_{j-1} (M 128, N d, K 128 keys; P in TMEM
-//     where S_{j-1} was, V read in place through an MN-major descriptor), so
-//     the tensor core computes the next scores while the softmax works;
-//   warps 0-3 -- softmax, one query row a thread (TMEM lane = row): first
-//     the row of Q (bf16) into TMEM, then per tile the row's 128 scores
-//     (tcgen05.ld), causal mask, running max, exp2, and bf16 P back into TMEM
-//     over the scores.  O is rescaled in TMEM only when the row max grows by
-//     more than 8 (log2 units): a stale max leaves O / l exact and keeps
-//     every P below 2^8.
-// The tensor core reads only K and V from shared memory (Q and P stay in
-// tensor memory): at 128 B/clock a tile's copies in and MMA reads out take
-// about as long as its MMAs.  MMAs execute in issue order, so S_{j+2} (issued
-// after P_j V_j) cannot overwrite P_j before it is read.
+//     pool view (zeros).  K_j is copied once S_A(j-2) and S_B(j-2) have read
+//     its slot, V_{j-1} once the P V products of tile j - 3 have;
+//   warp 9 -- TMEM allocation; lane 0 issues the MMAs.  Per key tile j and
+//     query tile t: O_t += P_t(j-1) V(j-1) (M 128, N d, K 128 keys; P in
+//     TMEM, V read in place through an MN-major descriptor), then S_t(j) =
+//     Q_t K_j^T (M 128, N 128, K = d; Q and K in shared memory) over the
+//     same TMEM columns -- MMAs run in issue order, so P_t(j-1) is read
+//     first.  One query tile's products run on the tensor core while the
+//     other tile's softmax works;
+//   warps 0-3 (tile A) and 4-7 (tile B) -- softmax, one query row a thread
+//     (TMEM lane = row): first the row of Q (bf16) into shared memory, then
+//     per key tile the row's 128 scores (tcgen05.ld), causal mask, running
+//     max, exp2, and bf16 P back into TMEM over the scores.  S_t(j) completes
+//     after P_t(j-1) V(j-1), so O_t is up to date when the scores arrive; it
+//     is rescaled in TMEM only when the row max grows by more than 8 (log2
+//     units): a stale max leaves O / l exact and keeps every P below 2^8.
+// Two softmax warps on each scheduler hide each other's dependent latency
+// (one warp a scheduler ran at 762 TF/s on the C4 prompt's last chunk).
 // At the end the O rows (tcgen05.ld) go to the split partials, merged in
 // split order as in the other attention kernels.  Scores are in log2 units
 // (log2 e folded into the query scale).  Every mbarrier wait is bounded
@@ -40,25 +42,27 @@ namespace dkv {
 
 uint32_t* device_error_word();
 
-constexpr int kPfRows = 128;          // query rows per CTA (MMA M, TMEM lanes)
+constexpr int kPfTile = 128;          // query rows per tile (MMA M, TMEM lanes)
+constexpr int kPfRows = 256;          // query rows per CTA: tiles A and B
 constexpr int kPfKeys = 128;          // keys per tile
-constexpr int kPfThreads = 192;       // 4 softmax warps, producer, MMA
-constexpr int kPfNst = 3;             // K and V ring depth
-constexpr int kPfTmemCols = 512;
-constexpr int kPfColO = 256;          // TMEM columns: S0 0-127 (P0 0-63), S1 128-255, O 256+, Q 384+
-constexpr int kPfColQ = 384;
+constexpr int kPfThreads = 320;       // 8 softmax warps (4 a query tile), producer, MMA
+constexpr int kPfNst = 2;             // K and V ring depth
+constexpr int kPfTmemCols = 512;      // per query tile t: S at 256 t (P over its first 64 columns), O at 256 t + 128
 constexpr int kPfSplitPages = 1024;   // page ids staged in shared memory
 constexpr float kPfRescale = 8.f;     // lazy-rescale threshold (log2 units)
 
-// Shared memory (from a 1024-byte aligned base): K slots [3][d/64][128 keys]
-// [64] then V slots (same arrangement), every 128 x 64 block in the 128-byte
-// swizzle (row r at r * 128 bytes, its 16-byte unit u at u ^ (r % 8)).
+// Shared memory (from a 1024-byte aligned base): Q of tiles A and B
+// [2][d/64][128 rows][64], K slots [2][d/64][128 keys][64], V slots (same
+// arrangement); every 128 x 64 block in the 128-byte swizzle (row r at
+// r * 128 bytes, its 16-byte unit u at u ^ (r % 8)).
 template <int D>
 struct PfGeo {
     static constexpr int CH = D / 64;
+    static constexpr int QT = CH * 16384;        // one query tile
     static constexpr int KVB = CH * 16384;       // one K (or V) tile
-    static constexpr int V0 = kPfNst * KVB;      // first V slot
-    static constexpr size_t SMEM = (size_t)2 * kPfNst * KVB + 1024;
+    static constexpr int K0 = 2 * QT;            // first K slot
+    static constexpr int V0 = K0 + kPfNst * KVB; // first V slot
+    static constexpr size_t SMEM = (size_t)V0 + kPfNst * KVB + 1024;
 };
 
 DKV_DEV uint32_t pf_pack(float lo, float hi) {
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     extern __shared__ uint8_t pf_raw[];
     uint8_t* sm = pf_raw + ((1024u - (smem_u32(pf_raw) & 1023u)) & 1023u);
     __shared__ __align__(8) uint64_t k_full[kPfNst], k_empty[kPfNst], v_full[kPfNst], v_empty[kPfNst];
-    __shared__ __align__(8) uint64_t s_full[2], p_full, o_done, drain;
+    __shared__ __align__(8) uint64_t s_full[2], p_full[2], o_done, drain;
     __shared__ uint32_t tmem_slot;
     __shared__ float ms[kPfRows], ls[kPfRows];
     __shared__ int32_t pages_s[kPfSplitPages];
@@ -131,6 +135,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     const int R = min(kPfRows, T * G - r0);
     const int HQ = a.n_kv * G;
     const size_t bhr = ((size_t)b * a.n_kv + h) * a.n_rb + rb;
+    const int wcap = (Geo::V0 + kPfNst * Geo::KVB) / 4;     // floats of the rings (the merge's scratch)
 
     pdl_trigger();
     pdl_wait();      // the queries and the chunk's cache rows come from earlier kernels
@@ -149,8 +154,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
             mypart[0] = -INFINITY;
             mypart[1] = 0.f;
         }
-        split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, reinterpret_cast<float*>(sm),
-                             (int)(2 * kPfNst * Geo::KVB / 4));
+        split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, reinterpret_cast<float*>(sm), wcap);
         return;
     }
 
@@ -161,15 +165,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(&p_full, 128);
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], 128);
+        }
         mbar_init(&o_done, 1);
         mbar_init(&drain, 1);
         fence_barrier_init();
         fence_async_shared();
     }
-    if (warp == 5) tmem_alloc(&tmem_slot, kPfTmemCols);
+    if (warp == 9) tmem_alloc(&tmem_slot, kPfTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -180,7 +185,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
 
     bool ok = true;
     int issued_k = 0, issued_v = 0;    // producer: tiles whose K / V copies were issued
-    if (warp == 4) {
+    if (warp == 8) {
         // ---------------- producer: the split's page ids, then per tile j the
         // copies of K_j and of V_{j-1}; lane p issues page p's boxes (one
         // lane's copies issue ~125 cycles apart), lane 0 arms the barrier
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
         const int kfree = min(qbase + r0 / G + 1, kend);
         auto issue = [&](int j, bool v) {
             const int slot = j % kPfNst;
-            uint8_t* dst = sm + (v ? Geo::V0 : 0) + slot * Geo::KVB;
+            uint8_t* dst = sm + (v ? Geo::V0 : Geo::K0) + slot * Geo::KVB;
             uint64_t* bar = v ? &v_full[slot] : &k_full[slot];
             if (lane == 0) mbar_expect_tx(bar, (uint32_t)Geo::KVB);
             __syncwarp();
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
         };
         for (int j = 0; j <= ntiles; ++j) {
             if (j < ntiles) {
-                // slot j % 3 was last read by S_{j-3}
+                // slot j % 2 was last read by S_A(j-2) and S_B(j-2)
                 if (j >= kPfNst && !__all_sync(0xffffffffu, mbar_wait(&k_empty[j % kPfNst],
                                                                       (uint32_t)((j / kPfNst - 1) & 1), a.err))) {
                     ok = false;
@@ -238,7 +243,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                 issued_k = j + 1;
             }
             if (j >= 1) {
-                const int i = j - 1;     // slot i % 3 was last read by P_{i-3} V_{i-3}
+                const int i = j - 1;     // slot i % 2 was last read by the P V products of tile i - 2
                 if (i >= kPfNst && !__all_sync(0xffffffffu, mbar_wait(&v_empty[i % kPfNst],
                                                                       (uint32_t)((i / kPfNst - 1) & 1), a.err))) {
                     ok = false;
@@ -248,15 +253,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                 issued_v = i + 1;
             }
         }
-    } else if (warp == 5) {
-        // ---------------- MMA issuer (the warp waits together, lane 0 issues)
-        const uint32_t ring_s = smem_u32(sm);
+    } else if (warp == 9) {
+        // ---------------- MMA issuer (the warp waits together, lane 0 issues).
+        // Per key tile j and query tile t (A = 0, B = 1): P_t(j-1) V(j-1),
+        // then S_t(j) over the same TMEM columns (MMAs run in issue order, so
+        // P_t(j-1) is read first), so one tile's product runs on the tensor
+        // core while the other tile's softmax works
+        const uint32_t q_s = smem_u32(sm), k_s0 = smem_u32(sm + Geo::K0), v_s0 = smem_u32(sm + Geo::V0);
         constexpr uint32_t idS = tc_idesc_n(kPfKeys, false), idO = tc_idesc_n(D, true);
-        auto issue_pv = [&](int i) -> bool {
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, a.err));
+        };
+        // V of tile i in place (the rest of a ragged last page zeroed)
+        auto v_ready = [&](int i) -> bool {
             const int slot = i % kPfNst;
-            if (!__all_sync(0xffffffffu, mbar_wait(&p_full, (uint32_t)(i & 1), a.err))) return false;
-            if (!__all_sync(0xffffffffu, mbar_wait(&v_full[slot], (uint32_t)((i / kPfNst) & 1), a.err)))
-                return false;
+            if (!wait_all(&v_full[slot], (uint32_t)((i / kPfNst) & 1))) return false;
             const int t0 = k0 + i * kPfKeys;
             if (kend - t0 < kPfKeys && (kend & 15) != 0) {
                 // the rest of the last page holds whatever the pool held
@@ -271,104 +282,128 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                 fence_async_shared();
                 __syncwarp();
             }
-            tc_fence_after();
-            if (lane == 0) {
-                const uint32_t v_s = ring_s + Geo::V0 + slot * Geo::KVB;
-                const uint32_t p_t = tmem + (uint32_t)((i & 1) * kPfKeys);
-#pragma unroll
-                for (int ks = 0; ks < kPfKeys / 16; ++ks)
-                    tc_mma_ts(tmem + kPfColO, p_t + ks * 8, sw128_desc_mn(v_s + ks * 2048, 16384), idO,
-                              (i | ks) != 0 ? 1u : 0u);
-                tc_commit(&o_done);
-                tc_commit(&v_empty[slot]);
-            }
-            __syncwarp();
             return true;
         };
-        named_sync(1, 160);      // Q is in TMEM
-        tc_fence_after();
-        for (int j = 0; j < ntiles; ++j) {
-            const int slot = j % kPfNst;
-            if (!__all_sync(0xffffffffu, mbar_wait(&k_full[slot], (uint32_t)((j / kPfNst) & 1), a.err))) {
+        auto issue_pv = [&](int t, int i) {
+            const uint32_t v_s = v_s0 + (i % kPfNst) * Geo::KVB;
+            const uint32_t base = tmem + (uint32_t)(t * 256);
+#pragma unroll
+            for (int ks = 0; ks < kPfKeys / 16; ++ks)
+                tc_mma_ts(base + 128, base + ks * 8, sw128_desc_mn(v_s + ks * 2048, 16384), idO,
+                          (i | ks) != 0 ? 1u : 0u);
+        };
+        auto issue_s = [&](int t, int j) {
+            const uint32_t k_s = k_s0 + (j % kPfNst) * Geo::KVB;
+            const uint32_t qt = q_s + t * Geo::QT;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk)
+                tc_mma_i(tmem + (uint32_t)(t * 256), sw128_desc(qt + (kk >> 2) * 16384 + (kk & 3) * 32),
+                         sw128_desc(k_s + (kk >> 2) * 16384 + (kk & 3) * 32), idS, kk != 0 ? 1u : 0u);
+            tc_commit(&s_full[t]);
+        };
+        named_sync(1, 288);      // Q is in shared memory
+        for (int j = 0; j < ntiles && ok; ++j) {
+            if (!wait_all(&k_full[j % kPfNst], (uint32_t)((j / kPfNst) & 1))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
+            if (j >= 1 && !v_ready(j - 1)) {
+                ok = false;
+                break;
+            }
+            for (int t = 0; t < 2; ++t) {
+                if (j >= 1 && !wait_all(&p_full[t], (uint32_t)((j - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    if (j >= 1) issue_pv(t, j - 1);
+                    issue_s(t, j);
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
             if (lane == 0) {
-                // S buffer j % 2 last held P_{j-2}: P_{j-2} V_{j-2} was issued
-                // before this (in-order execution)
-                const uint32_t k_s = ring_s + slot * Geo::KVB;
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    tc_mma_ts(tmem + (uint32_t)((j & 1) * kPfKeys), tmem + kPfColQ + kk * 8,
-                              sw128_desc(k_s + (kk >> 2) * 16384 + (kk & 3) * 32), idS, kk != 0 ? 1u : 0u);
-                tc_commit(&s_full[j & 1]);
-                tc_commit(&k_empty[slot]);
+                tc_commit(&k_empty[j % kPfNst]);               // S_A(j), S_B(j) read K_j
+                if (j >= 1) tc_commit(&v_empty[(j - 1) % kPfNst]);     // both P V of tile j - 1 read V_{j-1}
             }
             __syncwarp();
-            if (j >= 1 && !issue_pv(j - 1)) {
-                ok = false;
-                break;
-            }
         }
-        if (ok && ntiles > 0 && !issue_pv(ntiles - 1)) ok = false;
+        if (ok) {
+            const int i = ntiles - 1;
+            if (!v_ready(i)) ok = false;
+            for (int t = 0; t < 2 && ok; ++t) {
+                if (!wait_all(&p_full[t], (uint32_t)(i & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) issue_pv(t, i);
+                __syncwarp();
+            }
+            if (ok && lane == 0) tc_commit(&o_done);
+            __syncwarp();
+        }
     } else {
-        // ---------------- softmax: row r = threadIdx.x (TMEM lane r)
-        const int r = threadIdx.x;
-        const uint32_t lanes = tmem + ((uint32_t)(warp * 32) << 16);
+        // ---------------- softmax: query tile t (warps 4t .. 4t + 3), row rt
+        // of the tile = TMEM lane rt; CTA row cr = 128 t + rt
+        const int t = warp >> 2, rt = threadIdx.x & 127, cr = t * kPfTile + rt;
+        const uint32_t lanes = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const uint32_t sb = lanes + (uint32_t)(t * 256), ob = sb + 128;     // S (P over it), O
         {
-            // the row of Q: bf16 of q * scale * log2 e, two a column; rows >= R zero
+            // the row of Q in shared memory: bf16 of q * scale * log2 e, the
+            // tile's 128-byte swizzle; rows >= R zero
             const float sc = a.scale * kLog2e;
             const float* qrow =
-                r < R ? a.q + (((size_t)b * T + (r0 + r) / G) * HQ + h * G + (r0 + r) % G) * D : nullptr;
-#pragma unroll
-            for (int c0 = 0; c0 < D / 2; c0 += 32) {
-                uint32_t qv[32];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (qrow) x = __ldg(reinterpret_cast<const float4*>(qrow + 2 * (c0 + e)));
-                    qv[e] = pf_pack(x.x * sc, x.y * sc);
-                    qv[e + 1] = pf_pack(x.z * sc, x.w * sc);
+                cr < R ? a.q + (((size_t)b * T + (r0 + cr) / G) * HQ + h * G + (r0 + cr) % G) * D : nullptr;
+            uint8_t* qt = sm + t * Geo::QT;
+#pragma unroll 4
+            for (int u = 0; u < D / 8; ++u) {
+                float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+                if (qrow) {
+                    x0 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * u));
+                    x1 = __ldg(reinterpret_cast<const float4*>(qrow + 8 * u + 4));
                 }
-                tmem_st32(lanes + kPfColQ + c0, qv);
+                *reinterpret_cast<uint4*>(qt + (u >> 3) * 16384 + rt * 128 + (((u & 7) ^ (rt & 7)) << 4)) =
+                    make_uint4(pf_pack(x0.x * sc, x0.y * sc), pf_pack(x0.z * sc, x0.w * sc),
+                               pf_pack(x1.x * sc, x1.y * sc), pf_pack(x1.z * sc, x1.w * sc));
             }
-            tmem_wait_st();
-            tc_fence_before();
-            named_sync(1, 160);      // with the MMA warp
+            fence_async_shared();
+            named_sync(1, 288);      // with the MMA warp
         }
-        const int qp = r < R ? qbase + (r0 + r) / G : kend - 1;     // padding rows see every key
+        const int qp = cr < R ? qbase + (r0 + cr) / G : kend - 1;   // padding rows see every key
         const int lim = min(qp, kend - 1);                          // this row's last key
         float m = -INFINITY, l = 0.f;
         for (int j = 0; j < ntiles; ++j) {
-            const uint32_t sb = lanes + (uint32_t)((j & 1) * kPfKeys);
-            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (uint32_t)((j >> 1) & 1), a.err))) {
+            // S_t(j) done: and with it P_t(j-1) V(j-1), issued before it
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[t], (uint32_t)(j & 1), a.err))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t sr[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(sb + c * 32, sr[c]);
-            tmem_wait_ld();
             const int lc = lim - (k0 + j * kPfKeys);                  // last live column
-            if (lc < kPfKeys - 1) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (c * 32 + e > lc) sr[c][e] = __float_as_uint(-INFINITY);
-            }
-            // row max: 8 chains of three-input max
+            // pass 1: the row max, 32 scores at a time (8 chains of
+            // three-input max)
             float mx[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) mx[k] = __uint_as_float(sr[k >> 1][(k & 1) * 16]);
+            for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
+            for (int c = 0; c < 4; ++c) {
+                uint32_t sr[32];
+                tmem_ld32(sb + c * 32, sr);
+                tmem_wait_ld();
+                if (lc < kPfKeys - 1) {
 #pragma unroll
-                for (int e = 1; e < 16; e += 2)
-                    mx[k] = pf_max3(mx[k], __uint_as_float(sr[k >> 1][(k & 1) * 16 + e]),
-                                    e + 1 < 16 ? __uint_as_float(sr[k >> 1][(k & 1) * 16 + e + 1]) : mx[k]);
+                    for (int e = 0; e < 32; ++e)
+                        if (c * 32 + e > lc) sr[e] = __float_as_uint(-INFINITY);
+                }
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    const int k = 2 * c + (e >> 4);
+                    mx[k] = pf_max3(mx[k], __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+                }
+            }
             const float mn = fmaxf(m, pf_max3(pf_max3(mx[0], mx[1], mx[2]), pf_max3(mx[3], mx[4], mx[5]),
                                               fmaxf(mx[6], mx[7])));
             float alpha = 1.f;
@@ -377,68 +412,74 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                 m = mn;
             }
             const float msub = m == -INFINITY ? 0.f : m;
-            // exp2(s - m) two at a time: packed subtract and sum (f32x2)
+            // pass 2, 64 scores at a time: exp2(s - m) two at a time (packed
+            // subtract and sum), bf16 P into the 32 columns those scores
+            // held first (P block k over S columns 32k .. 32k + 31, read in
+            // this pass or the one before)
             const uint64_t mm = pf_pack2(msub, msub);
-            uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-            uint32_t pk[2][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float d0, d1;
-                    pf_unpack2(pf_sub2(pf_pack2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), mm), d0, d1);
-                    const float p0 = pf_ex2(d0), p1 = pf_ex2(d1);
-                    sum2[c] = pf_add2(sum2[c], pf_pack2(p0, p1));
-                    pk[c >> 1][(c & 1) * 16 + e / 2] = pf_pack(p0, p1);
-                }
-            float sum[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float a0, a1;
-                pf_unpack2(sum2[c], a0, a1);
-                sum[c] = a0 + a1;
-            }
-            l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
-            if (j >= 1) {
-                // P_{j-1} V_{j-1} has updated O (the waits stay in phase order)
-                if (!__all_sync(0xffffffffu, mbar_wait(&o_done, (uint32_t)((j - 1) & 1), a.err))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+            uint64_t sum2[2] = {0ull, 0ull};
+            uint32_t sr[2][32];
 #pragma unroll 1
-                    for (int c0 = 0; c0 < D; c0 += 32) {
-                        uint32_t o[32];
-                        tmem_ld32(lanes + kPfColO + c0, o);
-                        tmem_wait_ld();
+            for (int k = 0; k < 2; ++k) {
+                tmem_ld32(sb + 64 * k, sr[0]);
+                tmem_ld32(sb + 64 * k + 32, sr[1]);
+                tmem_wait_ld();
+                uint32_t pk[32];
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st32(lanes + kPfColO + c0, o);
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const int c = 2 * k + h2;
+                    if (lc < kPfKeys - 1) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e)
+                            if (c * 32 + e > lc) sr[h2][e] = __float_as_uint(-INFINITY);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        float d0, d1;
+                        pf_unpack2(pf_sub2(pf_pack2(__uint_as_float(sr[h2][e]), __uint_as_float(sr[h2][e + 1])), mm),
+                                   d0, d1);
+                        const float p0 = pf_ex2(d0), p1 = pf_ex2(d1);
+                        sum2[h2] = pf_add2(sum2[h2], pf_pack2(p0, p1));
+                        pk[h2 * 16 + e / 2] = pf_pack(p0, p1);
                     }
                 }
+                tmem_st32(sb + 32 * k, pk);
             }
-            // P_j over the first 64 columns of S_j
-            tmem_st32(sb, pk[0]);
-            tmem_st32(sb + 32, pk[1]);
-            tmem_wait_st();
+            float a0, a1, a2, a3;
+            pf_unpack2(sum2[0], a0, a1);
+            pf_unpack2(sum2[1], a2, a3);
+            l = l * alpha + ((a0 + a1) + (a2 + a3));
+            if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                // O_t holds P_t(j-1) V(j-1) (S_t(j) completed after it) and
+                // P_t(j) V(j) waits for this tile's P
+#pragma unroll 1
+                for (int c0 = 0; c0 < D; c0 += 32) {
+                    uint32_t o[32];
+                    tmem_ld32(ob + c0, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                    tmem_st32(ob + c0, o);
+                }
+            }
+            tmem_wait_st();      // P_t(j) is in TMEM (and any rescaled O)
             tc_fence_before();
-            mbar_arrive(&p_full);
+            mbar_arrive(&p_full[t]);
         }
-        if (ok && ntiles > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&o_done, (uint32_t)((ntiles - 1) & 1), a.err));
+        if (ok) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&o_done, 0u, a.err));
             tc_fence_after();
         }
         // ---- this split's partial row: (max in natural units, sum, O)
-        float* mypart = a.part + ((bhr * a.n_splits + s) * kPfRows + r) * PS;
-        const bool live = ok && ntiles > 0 && m != -INFINITY;
-        if (__all_sync(0xffffffffu, ok) && ntiles > 0) {
+        float* mypart = a.part + ((bhr * a.n_splits + s) * kPfRows + cr) * PS;
+        const bool live = ok && m != -INFINITY;
+        if (__all_sync(0xffffffffu, ok)) {
 #pragma unroll 1
             for (int c0 = 0; c0 < D; c0 += 32) {
                 uint32_t o[32];
-                tmem_ld32(lanes + kPfColO + c0, o);
+                tmem_ld32(ob + c0, o);
                 tmem_wait_ld();
-                if (live && r < R) {
+                if (live && cr < R) {
 #pragma unroll
                     for (int e = 0; e < 32; e += 2)
                         *reinterpret_cast<float2*>(mypart + 2 + c0 + e) =
@@ -446,7 +487,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
                 }
             }
         }
-        if (r < R) {
+        if (cr < R) {
             mypart[0] = live ? m * kLn2 : -INFINITY;
             mypart[1] = live ? l : 0.f;
         }
@@ -456,28 +497,27 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
     // for the copies and MMAs still in flight
     const bool all_ok = __syncthreads_and(ok) != 0;
     if (!all_ok) {
-        if (warp == 4 && lane == 0) {
+        if (warp == 8 && lane == 0) {
             for (int j = max(0, issued_k - kPfNst); j < issued_k; ++j)
                 mbar_wait(&k_full[j % kPfNst], (uint32_t)((j / kPfNst) & 1), nullptr);
             for (int j = max(0, issued_v - kPfNst); j < issued_v; ++j)
                 mbar_wait(&v_full[j % kPfNst], (uint32_t)((j / kPfNst) & 1), nullptr);
         }
-        if (warp == 5 && lane == 0) {
+        if (warp == 9 && lane == 0) {
             tc_commit(&drain);     // arrives once every MMA issued so far has completed
             mbar_wait(&drain, 0u, nullptr);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 9) {
         tc_fence_after();
         tmem_dealloc(tmem, kPfTmemCols);
     }
     // after a failure (error word set) every row of this split is empty, and
-    // the merge still runs so that the tickets stay consistent
-    // the drained rings hold the merge's per-(row, split) weights
-    split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, all_ok ? reinterpret_cast<float*>(sm) : nullptr,
-                         (int)(2 * kPfNst * Geo::KVB / 4));
+    // the merge still runs so that the tickets stay consistent; the drained
+    // rings hold the merge's per-(row, split) weights
+    split_merge<kPfRows>(a, bhr, b, h, R, r0, ms, ls, all_ok ? reinterpret_cast<float*>(sm) : nullptr, wcap);
 }
 
 // Host: the prefill launch of dkv_attn_full (rows > 64, bf16 pool in device

@@ -425,7 +425,7 @@ def run_gpu(args) -> None:
     torch.cuda.synchronize()
     prefill = {"tokens": B * (ctx - 1), "seconds": round(p0.elapsed_time(p1) / 1e3, 3),
                "tokens_per_s": round(B * (ctx - 1) / (p0.elapsed_time(p1) / 1e3), 1),
-               "basis": "engine.session(): chunked full-cache forwards of 512 tokens x the batch, no logits; "
+               "basis": "engine.session(): chunked full-cache forwards of max(512, 2048 / batch) tokens a sequence, no logits; "
                         "CUDA events (includes the host's launch of the chunks)"}
     setup_s = time.perf_counter() - t_setup
 

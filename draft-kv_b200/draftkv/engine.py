@@ -143,10 +143,12 @@ class DraftKVEngine:
         # drafter cache stays in HBM); verify streams it over the host link
         self.offload_full = False
         # prompt tokens per sequence in one prefill forward (prompts of 1024
-        # tokens or more; shorter ones take 64).  Measured on B200, 4 x 32767
-        # tokens of the Llama-3-8B shape: 14.4 s at 256, 13.2 s at 512, 13.1 s
-        # at 1024 (the causal attention over the prompt dominates)
+        # tokens or more; shorter ones take 64): at least prefill_chunk, and
+        # prefill_tokens over the batch, so that a forward's projections see
+        # ~2048 tokens (256-token GEMM tiles; 512 tokens a launch ran the
+        # Llama-3-8B shape's projections at 318 TF/s on B200)
         self.prefill_chunk = 512
+        self.prefill_tokens = 2048
 
         self.full_cache_factory = full_cache_factory
         self.gamma_max = gamma_max
@@ -179,7 +181,7 @@ class DraftKVEngine:
         m, B = self.model, st.B
         lens = [len(p) - 1 for p in prompts]
         L = max(lens) if lens else 0
-        CH = self.prefill_chunk if L >= 1024 else 64        # long prompts: fewer, larger chunks
+        CH = max(self.prefill_chunk, self.prefill_tokens // max(B, 1)) if L >= 1024 else 64
         tok = torch.zeros((B, max(L, 1)), dtype=torch.int32)
         for b, p in enumerate(prompts):
             if lens[b] > 0:

@@ -54,6 +54,18 @@ class BlockPool:
         self._allocated.add(b)
         return b
 
+    def allocate_many(self, n: int) -> list:
+        """n blocks in the order n calls of allocate() return them (the free
+        list's last-in first-out order), in one slice."""
+        if n > len(self._free):
+            raise BlockPoolExhausted(f"all {self.n_blocks} blocks of size {self.block_size} are in use")
+        if n <= 0:
+            return []
+        taken = self._free[-n:][::-1]
+        del self._free[-n:]
+        self._allocated.update(taken)
+        return taken
+
     def free(self, block: int) -> None:
         if block not in self._allocated:
             raise RuntimeError(f"double free of block {block}")
@@ -184,13 +196,16 @@ class PagedKVCache:
             raise BlockPoolExhausted(f"sequence needs {need} blocks > max_blocks_per_seq {self.max_pages}")
         for L in range(self.n_layers):
             tbl = self.block_tables[b][L]
-            while len(tbl) < need:
-                blk = self.pool.allocate()
-                idx = len(tbl)
-                tbl.append(blk)
-                if int(self.table_host[b, L, idx]) != blk:
-                    self.table_host[b, L, idx] = blk
-                    self._dirty = True
+            if len(tbl) >= need:
+                continue
+            i0 = len(tbl)
+            new = self.pool.allocate_many(need - i0)
+            tbl.extend(new)
+            row = self.table_host[b, L, i0:need]
+            arr = torch.tensor(new, dtype=row.dtype)
+            if not torch.equal(row, arr):
+                row.copy_(arr)
+                self._dirty = True
 
     def set_length(self, b: int, n: int) -> None:
         for L in range(self.n_layers):

@@ -198,7 +198,7 @@ class DraftKVEngine:
             tok_c = tok[:, c0:c1].contiguous()
             # no logits: the reference discards the prompt's (engine.py:133-134)
             m.forward_raw(st.full, None, tok_c.data_ptr(), c1 - c0, pos0, B, c1 - c0, None, work, CH,
-                          st.full.capacity_tokens)
+                          st.full.capacity_tokens, graph=False)
         for b in range(B):
             st.full.set_length(b, lens[b])
 

@@ -152,7 +152,7 @@ class DeviceDecoder:
 
     # ------------------------------------------------------------ forward
     def forward_raw(self, full, comp, tokens_ptr: int, tok_stride: int, pos0: "torch.Tensor", batch: int, T: int,
-                    logits: "torch.Tensor", work: "torch.Tensor", max_T: int, max_ctx: int) -> None:
+                    logits: "torch.Tensor", work: "torch.Tensor", max_T: int, max_ctx: int, graph: bool = True) -> None:
         """One native forward for `batch` sequences x T tokens (device pointers);
         `logits` None runs no final norm and head (a prefill chunk).
 
@@ -160,7 +160,9 @@ class DeviceDecoder:
         the drafter's per-layer configs) have been seen before is replayed as a
         CUDA graph: the second call with given arguments captures it, later
         calls replay it.  The token, position and cache contents are read at
-        replay time; only the launch parameters are frozen."""
+        replay time; only the launch parameters are frozen.  `graph` False
+        launches eagerly (prompt chunks: a capture syncs the device and costs
+        more than the few launches a replay would save)."""
         step = _lib.StepS(batch, T, tokens_ptr, tok_stride, pos0.data_ptr(), None if logits is None else logits.data_ptr(),
                           work.data_ptr(), work.numel(), max_ctx, max_T)
         fs = None if full is None else full.struct()        # (syncs a changed page table first)
@@ -170,7 +172,7 @@ class DeviceDecoder:
             _lib.call("dkv_forward", C.byref(self._s), None if fs is None else C.byref(fs),
                       None if cs is None else C.byref(cs), C.byref(step), _lib.stream_ptr())
 
-        if not self.use_graphs or _lib.prof_active:
+        if not (graph and self.use_graphs) or _lib.prof_active:
             run()
             return
         key = (tuple(getattr(step, f) for f, _ in step._fields_),

@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
 // leaves a CTA a dozen tiles against its fixed costs and the merge of the
 // last one 37 splits to read: 348 TF/s there, against 863 at 8192-key splits
 // on 4 x 32k); partials and tickets come from the attention work buffer.
-constexpr int kPfMinSplit = 8192;
+constexpr int kPfMinSplit = 8192;     // the same floor as the forward's scratch sizing (forward.cu)
 
 int attn_prefill_tc(AttnArgs& a, dkv_dims dims, const KvMaps& maps, void* work, size_t work_bytes, int max_keys,
                     cudaStream_t st) {

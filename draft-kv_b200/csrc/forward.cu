@@ -14,6 +14,7 @@ size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_
 int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st);
 int gemm_entry(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K, const dkv_epilogue* epi,
                void* work, size_t work_bytes, void* stream, bool fill);
+constexpr int kPromptMinSplit = 8192;    // keys per split of bf16 attention over more than 64 rows
 
 // RMSNorm fused into the GEMMs (bf16 Llama-family models): the norm before
 // the QKV, gate/up and head projections costs no launch of its own.
@@ -40,7 +41,16 @@ size_t dkv::forward_work(const dkv_model* m, int batch, int T, int max_ctx, int 
     g = std::max(g, dkv_gemm_work_bytes(round128(m->d_model), N, m->d_ff, m->dtype));
     g = std::max(g, dkv_gemm_work_bytes(m->vocab_pad, N, m->d_model, m->dtype));
     dkv_dims dims{m->n_layers, m->n_kv, m->d_head, batch};
-    const size_t a = dkv_attn_work_bytes(dims, m->n_heads / m->n_kv, T, max_ctx, m->split_keys, comp_cap);
+    // attention scratch: up to 64 query rows (decode, verify) at the model's
+    // split; more rows (prompt chunks) in bf16 take splits of at least
+    // kPromptMinSplit keys (attention_prefill.cu), far fewer partials
+    const int G = m->n_heads / m->n_kv;
+    const int sk = m->split_keys > 0 ? m->split_keys : 512;
+    size_t a = dkv_attn_work_bytes(dims, G, std::min(T, std::max(1, 64 / G)), max_ctx, sk, comp_cap);
+    if (T * G > 64) {
+        const int sk_rows = m->dtype == DKV_BF16 ? std::max(kPromptMinSplit, (sk + 127) / 128 * 128) : sk;
+        a = std::max(a, dkv_attn_work_bytes(dims, G, T, max_ctx, sk_rows, comp_cap));
+    }
     if (attn_bytes) *attn_bytes = a;
     if (gemm_bytes) *gemm_bytes = g;
     size_t b = 0;

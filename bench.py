@@ -907,7 +907,7 @@ def run_kernel(args) -> None:
       verify-attn  full-cache attention for T query tokens per sequence
       prefill-attn the same for a prompt chunk (T = 512 tokens at the end of
                    the context, pages in the block pool's allocation order,
-                   8192-key splits): the tcgen05 prefill kernel, in TF/s
+                   16384-key splits): the tcgen05 prefill kernel, in TF/s
       gemm         weight-streaming GEMM, M x K weights, N tokens
       gemm-layer   the four projections of a decoder layer (Llama-3-8B shape:
                    QKV, O, gate/up, down) back to back as the forward launches
@@ -997,7 +997,7 @@ def run_kernel(args) -> None:
         full = full_cache()
         prefill = args.kernel == "prefill-attn"
         T = args.T or (512 if prefill else 9)
-        split = args.split or (8192 if prefill else 512)
+        split = args.split or (16384 if prefill else 512)
         work = torch.zeros(int(_lib.load().dkv_attn_work_bytes(full.dims(), G, T, ctx + 64, split, 0)),
                            dtype=torch.uint8, device="cuda")
         qv = torch.randn((B * T, n_kv * G, d), device="cuda")
@@ -1120,7 +1120,7 @@ def main() -> None:
     ap.add_argument("--K", type=int, default=4096)
     ap.add_argument("--N", type=int, default=4)
     ap.add_argument("--iters", type=int, default=10)
-    ap.add_argument("--split", type=int, default=None, help="keys per split (verify-attn 512, prefill-attn 8192)")
+    ap.add_argument("--split", type=int, default=None, help="keys per split (verify-attn 512, prefill-attn 16384)")
     ap.add_argument("--no-shuffle", action="store_true", help="kernel mode: keep the page table in allocation order")
     args = ap.parse_args()
     if args.kernel:

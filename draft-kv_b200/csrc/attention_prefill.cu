@@ -525,9 +525,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
 // of the key range: the caller's split rounded up to 128 keys, at least
 // kPfMinSplit (the decode-time split -- 1792 keys for one sequence at 64k --
 // leaves a CTA a dozen tiles against its fixed costs and the merge of the
-// last one 37 splits to read: 348 TF/s there, against 863 at 8192-key splits
-// on 4 x 32k); partials and tickets come from the attention work buffer.
-constexpr int kPfMinSplit = 8192;     // the same floor as the forward's scratch sizing (forward.cu)
+// last one 37 splits to read: 348 TF/s there.  Measured on B200: 8192-key
+// splits 863 TF/s on 4 x 32k and 924 on 1 x 64k with 2048-token chunks,
+// 16384-key splits 882 and 997); partials and tickets come from the
+// attention work buffer.
+constexpr int kPfMinSplit = 16384;    // the same floor as the forward's scratch sizing (forward.cu)
 
 int attn_prefill_tc(AttnArgs& a, dkv_dims dims, const KvMaps& maps, void* work, size_t work_bytes, int max_keys,
                     cudaStream_t st) {

@@ -14,7 +14,7 @@ size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_
 int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st);
 int gemm_entry(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K, const dkv_epilogue* epi,
                void* work, size_t work_bytes, void* stream, bool fill);
-constexpr int kPromptMinSplit = 8192;    // keys per split of bf16 attention over more than 64 rows
+constexpr int kPromptMinSplit = 16384;   // keys per split of bf16 attention over more than 64 rows
 
 // RMSNorm fused into the GEMMs (bf16 Llama-family models): the norm before
 // the QKV, gate/up and head projections costs no launch of its own.

@@ -527,7 +527,7 @@ def test_full_attention_matches_torch_and_decode(dtype, G, d):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("G", [1, 4])
-@pytest.mark.parametrize("n,T,split", [(700, 700, 3648), (1000, 37, 256), (4100, 300, 1024), (4100, 300, 128)])
+@pytest.mark.parametrize("n,T,split", [(700, 700, 3648), (1000, 37, 256), (4100, 300, 1024), (40000, 300, 128)])
 def test_prefill_attention_matches_torch(d, G, n, T, split):
     """The tcgen05 prefill kernel (more than 64 query rows, bf16 pool in
     device memory): causal GQA attention of T new tokens at positions
@@ -537,10 +537,10 @@ def test_prefill_attention_matches_torch(d, G, n, T, split):
     splits and lazy rescale) moves single outputs by up to 1.24e-2 and the
     mean by 2.5e-4 to 5.8e-4.  Cases: a whole 700-token prompt (ragged last
     row block, one split), 37 tokens over 1000 keys in 256-key splits (rows
-    whose split starts past their position), 300 tokens over 4100 keys in
-    1024- and 128-key splits (35 splits: the merge stages its weights in the
-    drained ring; splits past the rows' positions exit early); every context
-    ends inside a page whose unused rows hold NaN."""
+    whose split starts past their position), 300 tokens over 4100 keys, and
+    over 40000 keys (the prompt kernel's splits are at least 16384 keys: 3
+    splits merged, through the weights staged in the drained ring); every
+    context ends inside a page whose unused rows hold NaN."""
     from draftkv import PagedKVCache
     L = lib()
     n_kv = 2

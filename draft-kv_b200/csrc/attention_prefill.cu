@@ -523,18 +523,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) attn_prefill_tc_kernel(const __
 // Host: the prefill launch of dkv_attn_full (rows > 64, bf16 pool in device
 // memory with 16-key pages, d 64 or 128, 16-byte aligned queries).  Splits
 // of the key range: the caller's split rounded up to 128 keys, at least
-// kPfMinSplit (the decode-time split -- 1792 keys for one sequence at 64k --
+// kPromptMinSplit (the decode-time split -- 1792 keys for one sequence at 64k --
 // leaves a CTA a dozen tiles against its fixed costs and the merge of the
 // last one 37 splits to read: 348 TF/s there.  Measured on B200: 8192-key
 // splits 863 TF/s on 4 x 32k and 924 on 1 x 64k with 2048-token chunks,
 // 16384-key splits 882 and 997); partials and tickets come from the
 // attention work buffer.
-constexpr int kPfMinSplit = 16384;    // the same floor as the forward's scratch sizing (forward.cu)
-
 int attn_prefill_tc(AttnArgs& a, dkv_dims dims, const KvMaps& maps, void* work, size_t work_bytes, int max_keys,
                     cudaStream_t st) {
     const int R = a.T * a.group;
-    a.split = std::max(kPfMinSplit, (a.split + kPfKeys - 1) / kPfKeys * kPfKeys);
+    a.split = std::max(kPromptMinSplit, (a.split + kPfKeys - 1) / kPfKeys * kPfKeys);
     a.n_rb = (R + kPfRows - 1) / kPfRows;
     a.n_splits = std::max(1, (max_keys + a.split - 1) / a.split);
     const size_t n_tk = (size_t)dims.batch * dims.n_kv * a.n_rb;

@@ -672,9 +672,9 @@ int attn_full_tc(AttnArgs& a, dkv_dims dims, void* work, size_t work_bytes, int 
         }
     }
     // more than 64 rows (a prompt chunk over a host-resident pool): splits of
-    // at least 16384 keys, as the tcgen05 prefill kernel takes (the forward's
-    // scratch is sized for that)
-    if (R > kAttnRB && a.split < 16384) a.split = 16384;
+    // at least kPromptMinSplit keys, as the tcgen05 prefill kernel takes (the
+    // forward's scratch is sized for that)
+    if (R > kAttnRB && a.split < kPromptMinSplit) a.split = kPromptMinSplit;
     a.n_rb = R <= kAttnRB ? (R + kKqRows - 1) / kKqRows : (R + kAttnRB - 1) / kAttnRB;
     a.n_splits = (max_keys + a.split - 1) / a.split;
     if (a.n_splits < 1) a.n_splits = 1;

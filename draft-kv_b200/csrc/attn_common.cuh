@@ -49,6 +49,11 @@ struct AttnArgs {
 };
 
 constexpr int kAttnRB = 64;   // query rows (token x group head) per CTA
+// Keys per split, at least, of bf16 attention over more than kAttnRB query
+// rows (prompt chunks: no row of theirs is compared with a decode row): the
+// tcgen05 prefill kernel and the host-pool fallback take it, and the
+// forward's work buffer is sized for it
+constexpr int kPromptMinSplit = 16384;
 
 // Tensor maps of the K and V pools for the copy-engine-fed kernels: 4-D views
 // {d, 16 page rows, n_kv, n_pages} with 128-byte swizzle; k / v copy a box of

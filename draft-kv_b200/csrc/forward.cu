@@ -6,7 +6,7 @@
 // captured into one CUDA graph per (shape, config).
 #include <algorithm>
 
-#include "common.cuh"
+#include "attn_common.cuh"
 
 namespace dkv {
 size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_cap, size_t* attn_bytes,
@@ -14,7 +14,6 @@ size_t forward_work(const dkv_model* m, int batch, int T, int max_ctx, int comp_
 int norm_prep(const float* h, int N, int dm, const float* w, void* x, float* part, int ld, cudaStream_t st);
 int gemm_entry(const void* x, int x_dtype, const void* w, int w_dtype, int M, int N, int K, const dkv_epilogue* epi,
                void* work, size_t work_bytes, void* stream, bool fill);
-constexpr int kPromptMinSplit = 16384;   // keys per split of bf16 attention over more than 64 rows
 
 // RMSNorm fused into the GEMMs (bf16 Llama-family models): the norm before
 // the QKV, gate/up and head projections costs no launch of its own.
@@ -43,7 +42,7 @@ size_t dkv::forward_work(const dkv_model* m, int batch, int T, int max_ctx, int 
     dkv_dims dims{m->n_layers, m->n_kv, m->d_head, batch};
     // attention scratch: up to 64 query rows (decode, verify) at the model's
     // split; more rows (prompt chunks) in bf16 take splits of at least
-    // kPromptMinSplit keys (attention_prefill.cu), far fewer partials
+    // kPromptMinSplit keys, far fewer partials
     const int G = m->n_heads / m->n_kv;
     const int sk = m->split_keys > 0 ? m->split_keys : 512;
     size_t a = dkv_attn_work_bytes(dims, G, std::min(T, std::max(1, 64 / G)), max_ctx, sk, comp_cap);

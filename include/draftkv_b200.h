@@ -204,8 +204,12 @@ DKV_API int dkv_comp_read(const dkv_comp_cache* comp, dkv_dims dims, int b, int 
  * sequence b, T query tokens at positions pos0[b] .. pos0[b]+T-1, each of the
  * n_kv*group heads attends keys 0 .. its own position (causal).
  * q [batch*T][n_kv*group][d] f32; out [batch*T][n_kv*group*d] (out_dtype).
- * Keys are split in fixed chunks of split_keys positions so that a row's
- * result does not depend on T (verify row i == decode at that position). */
+ * Up to 64 query rows (T * group <= 64: decode, verify) keys are split in
+ * fixed chunks of split_keys positions and a row's result does not depend on
+ * T (verify row i == decode at that position, bit for bit).  More rows (a
+ * prompt chunk) in bf16 take the prompt kernel with splits of at least
+ * 16384 keys: within bf16 rounding of the same attention, not bitwise equal
+ * to the rows of a decode call. */
 DKV_API int dkv_attn_full(const dkv_full_cache* full, dkv_dims dims, int layer, int group, int T,
                   const float* d_q, const int32_t* d_pos0, void* d_out, int out_dtype,
                   int split_keys, void* d_work, size_t work_bytes, void* stream);

@@ -381,7 +381,10 @@ typedef struct {
     const int32_t* pos0;          /* [batch] position of token t=0 */
     float* logits;                /* [batch*T][vocab_pad] f32, or NULL: no final norm and head
                                      (a prefill that only writes the cache; the reference discards
-                                     those logits, draftkv/engine.py:133-134) */
+                                     those logits, draftkv/engine.py:133-134).  With NULL each
+                                     projection takes the K split that fills the GPU for batch*T
+                                     tokens, so the cache rows it writes match a logits forward's
+                                     within bf16 rounding, not bit for bit */
     /* scratch (caller allocates dkv_forward_work_bytes) */
     void* work;
     size_t work_bytes;
